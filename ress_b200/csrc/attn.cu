@@ -1,0 +1,452 @@
+// attn.cu -- block-sparse attention on the sm_100a tensor cores.
+//
+// Semantics (reference: SpargeAttn's qk_int8_sv_f16_accum_f16_block_sparse_
+// attn_inst_buf_with_pv_threshold as called by run_block_sparse_kernel,
+// src/ress/models/attention.py:217-243): for each (head, 128-query block)
+// row and its ascending list of kept 64-key blocks,
+//     S = (q8 k8^T) * qscale[qb] * kscale[kb],  P = softmax(S * sm_scale),
+//     O = P V,
+// non-causal, keys past Tk masked.  Q and K arrive as per-block int8 with
+// fp32 scales (ress_score_quant), V as fp16.
+//
+// One CTA per row, 6 warps:
+//   warp 0      TMA producer: Q tile once, then K/V tiles of the listed
+//               blocks through an NS-stage ring (cp.async.bulk.tensor);
+//               also allocates / frees the CTA's tensor memory.
+//   warp 1      MMA issuer (one thread): S_j = Q K_j^T with
+//               tcgen05.mma kind::i8 into a TMEM double buffer, and
+//               PV_j = P_j V_j with kind::f16 (fp16 x fp16 -> fp32) into a
+//               second TMEM double buffer.
+//   warps 2-5   softmax: thread = query row = TMEM lane.  Reads S_j with
+//               tcgen05.ld, keeps the running max / sum, writes P_j (fp16)
+//               into shared memory in the 128B-swizzled K-major layout the
+//               MMA reads, and folds PV_{j-1} into fp32 registers.
+// Every mbarrier wait is bounded (~2 s); on expiry the CTA raises an abort
+// flag, records RESS_STATUS_ATTN_WAIT_TIMEOUT, drains its own in-flight
+// copies and MMAs, frees its tensor memory and exits.
+// No TMA multicast is used.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <climits>
+
+#include "common.cuh"
+
+namespace ress {
+namespace attn {
+
+constexpr int NT = 192;
+constexpr int NS = 4;                  // K/V ring stages
+constexpr int Q_BYTES = 128 * 64;      // int8
+constexpr int K_BYTES = 64 * 64;       // int8
+constexpr int V_BYTES = 64 * 64 * 2;   // fp16
+constexpr int P_BYTES = 128 * 64 * 2;  // fp16
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + Q_BYTES;
+constexpr int OFF_V = OFF_K + NS * K_BYTES;
+constexpr int OFF_P = OFF_V + NS * V_BYTES;
+constexpr int SMEM_TILES = OFF_P + 2 * P_BYTES;
+constexpr int SMEM_BYTES = SMEM_TILES + 1024;  // + alignment slack
+constexpr uint32_t TMEM_COLS = 256;            // S[2] (64 each) + O[2] (64 each)
+constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
+
+// ------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false when the CTA aborted or this wait expired.
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                         int32_t *status) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (mbar_try_wait(addr, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > TIMEOUT_NS) {
+            *abort_flag = 1;
+            atomicOr(status, RESS_STATUS_ATTN_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
+// Warp-uniform variant for warps that go on to execute .sync.aligned
+// tcgen05 instructions: every lane waits, and the warp proceeds only if all
+// lanes saw the phase complete.
+__device__ __forceinline__ bool wait_bar_warp(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                              int32_t *status) {
+    const bool ok = wait_bar(bar, parity, abort_flag, status);
+    return __all_sync(0xffffffffu, ok);
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint64_t *bar, int x, int y,
+                                            int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+            "r"(dst),
+        "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// UMMA shared-memory descriptor (sm100 format: version 1 at bits 46-47,
+// layout type at bits 61-63: 2 = 128B swizzle, 4 = 64B swizzle).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)layout << 61;
+    return d;
+}
+constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
+
+// Instruction descriptors (M = 128, N = 64).
+//   kind::i8 : D s32 (bits 4-5 = 2), A/B signed (bits 7, 10), both K-major.
+//   kind::f16: D f32 (1), A/B f16 (0), A K-major, B MN-major (bit 16).
+constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t IDESC_F16 = (1u << 4) | (1u << 16) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+
+struct Bars {
+    uint64_t q_full;
+    uint64_t kv_full[NS], kv_empty[NS];
+    uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
+    uint64_t mma_done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+__global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const float *__restrict__ qscale,
+    const float *__restrict__ kscale, int nqb, int nkb, int Tq, int Tk, const int32_t *__restrict__ lists,
+    const int32_t *__restrict__ counts, int list_width, float sm_scale_log2, float *__restrict__ out,
+    long long out_sh, long long out_st, int out_hw, int out_special, int32_t *__restrict__ status) {
+    extern __shared__ unsigned char dyn_raw[];
+    __shared__ Bars B;
+    unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)dyn_raw + 1023) & ~(uintptr_t)1023);
+    const uint32_t sQ = smem_u32(smem + OFF_Q);
+    const uint32_t sK = smem_u32(smem + OFF_K);
+    const uint32_t sV = smem_u32(smem + OFF_V);
+    const uint32_t sP = smem_u32(smem + OFF_P);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x;
+    const int bh = row / nqb, qb = row - bh * nqb;
+    const int cnt = min(counts[row], list_width);
+    const int32_t *lst = lists + (size_t)row * list_width;
+    volatile int *abort_flag = &B.abort_flag;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&B.q_full, 1);
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&B.kv_full[i], 1);
+            mbar_init(&B.kv_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&B.s_full[i], 1);
+            mbar_init(&B.s_free[i], 128);
+            mbar_init(&B.p_full[i], 128);
+            mbar_init(&B.o_full[i], 1);
+            mbar_init(&B.o_free[i], 128);
+        }
+        mbar_init(&B.mma_done, 1);
+        B.abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B.tmem_base)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = B.tmem_base;
+    const uint32_t tS = tmem, tO = tmem + 128;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0 && cnt > 0) {
+            mbar_expect_tx(&B.q_full, Q_BYTES);
+            tma_load_3d(sQ, &tm_q, &B.q_full, 0, qb * 128, bh);
+            int j = 0;
+            for (; j < cnt; ++j) {
+                const int st = j % NS;
+                if (j >= NS && !wait_bar(&B.kv_empty[st], ((j - NS) / NS) & 1, abort_flag, status)) break;
+                const int kb = lst[j];
+                mbar_expect_tx(&B.kv_full[st], K_BYTES + V_BYTES);
+                tma_load_3d(sK + st * K_BYTES, &tm_k, &B.kv_full[st], 0, kb * 64, bh);
+                tma_load_3d(sV + st * V_BYTES, &tm_v, &B.kv_full[st], 0, kb * 64, bh);
+            }
+            // drain: the last load issued on each stage must have landed
+            // before the CTA may exit (already true on the normal path)
+            const int issued = j;
+            for (int st = 0; st < NS && st < issued; ++st) {
+                const int last = issued - 1 - ((issued - 1 - st) % NS);
+                const uint32_t addr = smem_u32(&B.kv_full[st]);
+                const uint64_t t0 = globaltimer();
+                while (!mbar_try_wait(addr, (last / NS) & 1) && globaltimer() - t0 < TIMEOUT_NS) {
+                }
+            }
+            {
+                const uint32_t addr = smem_u32(&B.q_full);
+                const uint64_t t0 = globaltimer();
+                while (!mbar_try_wait(addr, 0) && globaltimer() - t0 < TIMEOUT_NS) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0 && cnt > 0) {
+            bool ok = wait_bar(&B.q_full, 0, abort_flag, status);
+            auto issue_pv = [&](int i) -> bool {
+                const int pb = i & 1;
+                if (!wait_bar(&B.p_full[pb], (i >> 1) & 1, abort_flag, status)) return false;
+                if (i >= 2 && !wait_bar(&B.o_free[pb], ((i - 2) >> 1) & 1, abort_flag, status)) return false;
+                fence_after();
+                const uint32_t pa = sP + pb * P_BYTES;
+                const uint32_t va = sV + (i % NS) * V_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t ad = make_desc(pa + kk * 32, 16, 1024, LAYOUT_SW128);
+                    const uint64_t bd = make_desc(va + kk * 2048, 8192, 1024, LAYOUT_SW128);
+                    mma_f16(tO + pb * 64, ad, bd, IDESC_F16, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&B.o_full[pb]);
+                mma_commit(&B.kv_empty[i % NS]);
+                return true;
+            };
+            for (int j = 0; ok && j < cnt; ++j) {
+                const int st = j % NS, sb = j & 1;
+                if (!wait_bar(&B.kv_full[st], (j / NS) & 1, abort_flag, status)) break;
+                if (j >= 2 && !wait_bar(&B.s_free[sb], ((j - 2) >> 1) & 1, abort_flag, status)) break;
+                fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+                    const uint64_t ad = make_desc(sQ + kk * 32, 16, 512, LAYOUT_SW64);
+                    const uint64_t bd = make_desc(sK + st * K_BYTES + kk * 32, 16, 512, LAYOUT_SW64);
+                    mma_i8(tS + sb * 64, ad, bd, IDESC_I8, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&B.s_full[sb]);
+                if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+                if (j == cnt - 1 && !issue_pv(j)) { ok = false; break; }
+            }
+            // all MMAs issued by this thread complete before TMEM is freed
+            mma_commit(&B.mma_done);
+            const uint32_t addr = smem_u32(&B.mma_done);
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(addr, 0) && globaltimer() - t0 < TIMEOUT_NS) {
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ softmax
+        const int quad = warp & 3;                 // TMEM lane quadrant of this warp
+        const int r = quad * 32 + lane;            // query row within the block
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const float qs = qscale[(size_t)bh * nqb + qb];
+        float o[HD];
+#pragma unroll
+        for (int i = 0; i < HD; ++i) o[i] = 0.0f;
+        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+        bool ok = true;
+        const uint32_t prow = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
+        auto fold = [&](int i, float alpha) -> bool {
+            const int pb = i & 1;
+            if (!wait_bar_warp(&B.o_full[pb], (i >> 1) & 1, abort_flag, status)) return false;
+            fence_after();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[16];
+                tmem_ld16(tO + pb * 64 + c * 16 + lane_addr, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int t = 0; t < 16; ++t) o[c * 16 + t] = fmaf(o[c * 16 + t], alpha, __uint_as_float(v[t]));
+            }
+            fence_before();
+            mbar_arrive(&B.o_free[pb]);
+            return true;
+        };
+        for (int j = 0; j < cnt; ++j) {
+            const int sb = j & 1;
+            const int kb = lst[j];
+            const float c = qs * kscale[(size_t)bh * nkb + kb] * sm_scale_log2;
+            const int nvalid = min(64, Tk - kb * 64);
+            if (!wait_bar_warp(&B.s_full[sb], (j >> 1) & 1, abort_flag, status)) { ok = false; break; }
+            fence_after();
+            int smax = INT_MIN;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t v[16];
+                tmem_ld16(tS + sb * 64 + ch * 16 + lane_addr, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int t = 0; t < 16; ++t)
+                    if (ch * 16 + t < nvalid) smax = max(smax, (int)v[t]);
+            }
+            const float mx = c * (float)smax;
+            const float m_new = fmaxf(m, mx);
+            const float alpha = exp2f(m - m_new);
+            float lsum = 0.0f;
+            const uint32_t pbase = sP + sb * P_BYTES + prow;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t v[16];
+                tmem_ld16(tS + sb * 64 + ch * 16 + lane_addr, v);
+                tmem_wait_ld();
+                uint32_t h[8];
+#pragma unroll
+                for (int t = 0; t < 16; t += 2) {
+                    float p0 = (ch * 16 + t < nvalid) ? exp2f(fmaf(c, (float)(int)v[t], -m_new)) : 0.0f;
+                    float p1 = (ch * 16 + t + 1 < nvalid) ? exp2f(fmaf(c, (float)(int)v[t + 1], -m_new)) : 0.0f;
+                    __half2 hp = __floats2half2_rn(p0, p1);
+                    lsum += __low2float(hp) + __high2float(hp);
+                    h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
+                }
+                // two 16-byte chunks (8 keys each) -> swizzled positions
+                const uint32_t c0 = (uint32_t)(2 * ch), c1 = c0 + 1;
+                const uint32_t a0 = pbase + ((c0 ^ (uint32_t)(r & 7)) << 4);
+                const uint32_t a1 = pbase + ((c1 ^ (uint32_t)(r & 7)) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a0), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+                             : "memory");
+                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a1), "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7])
+                             : "memory");
+            }
+            fence_before();
+            mbar_arrive(&B.s_free[sb]);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&B.p_full[sb]);
+            l = l * alpha + lsum;
+            m = m_new;
+            if (j >= 1 && !fold(j - 1, alpha_prev)) { ok = false; break; }
+            alpha_prev = alpha;
+        }
+        if (ok && cnt > 0) ok = fold(cnt - 1, alpha_prev);
+        const int t = qb * 128 + r;
+        if (t < Tq) {
+            const long long tt = (long long)(t / out_hw) * (out_hw + out_special) + out_special + (t % out_hw);
+            float *dst = out + (size_t)bh * out_sh + tt * out_st;
+            const float inv = (ok && cnt > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+#pragma unroll
+            for (int i = 0; i < HD; i += 4)
+                *reinterpret_cast<float4 *>(dst + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+        }
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
+// ------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+static bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, int T, int BH,
+                     int box_rows, CUtensorMapSwizzle sw) {
+    auto enc = get_encode();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {64, (cuuint64_t)T, (cuuint64_t)BH};
+    cuuint64_t strides[2] = {(cuuint64_t)64 * elem_bytes, (cuuint64_t)T * 64 * elem_bytes};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace attn
+}  // namespace ress
+
+using namespace ress;
+
+extern "C" int ress_sparse_attn(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
+                                const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
+                                const int32_t *counts, int list_width, float sm_scale, float *out,
+                                long long out_sh, long long out_st, int out_hw, int out_special,
+                                int32_t *status, ress_stream_t stream) {
+    if (!q8 || !qscale || !k8 || !kscale || !v16 || !lists || !counts || !out || !status) return RESS_E_ARG;
+    if (BH <= 0 || Tq <= 0 || Tk <= 0 || list_width <= 0 || out_hw <= 0 || out_special < 0) return RESS_E_ARG;
+    if (((uintptr_t)q8 | (uintptr_t)k8 | (uintptr_t)v16) & 15) return RESS_E_ARG;
+    if (((uintptr_t)out & 15) || (out_st & 3) || (out_sh & 3)) return RESS_E_ARG;
+    if ((long long)BH * Tk * 64 * 2 > (1ll << 40)) return RESS_E_SHAPE;
+    CUtensorMap tq, tk, tv;
+    if (!attn::make_map(&tq, q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Tq, BH, 128, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !attn::make_map(&tk, k8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Tk, BH, 64, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !attn::make_map(&tv, v16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Tk, BH, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+        return RESS_E_NO_DEVICE;
+    const int nqb = (Tq + 127) / 128, nkb = (Tk + 63) / 64;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(attn::sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 attn::SMEM_BYTES) != cudaSuccess)
+            return RESS_E_LAUNCH;
+        attr_set = true;
+    }
+    const float log2e = 1.4426950408889634f;
+    attn::sparse_attn_kernel<<<BH * nqb, attn::NT, attn::SMEM_BYTES, (cudaStream_t)stream>>>(
+        tq, tk, tv, qscale, kscale, nqb, nkb, Tq, Tk, lists, counts, list_width, sm_scale * log2e, out, out_sh,
+        out_st, out_hw, out_special, status);
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}

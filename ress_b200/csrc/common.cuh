@@ -1,0 +1,231 @@
+// common.cuh -- device helpers shared by the sm_100a kernels.
+//
+// Exactness: the selection kernels must produce the same bits as the CPU
+// oracle, so every floating-point step on that path is written with the
+// IEEE round-to-nearest intrinsics (__fadd_rn, __fmul_rn, __fmaf_rn, ...),
+// which the compiler never contracts or reorders.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ress_sm100.h"
+
+namespace ress {
+
+constexpr int HD = 64;      // head dimension (fixed by the kernels)
+constexpr int KS_Q = 128;   // query block (reference attention.py:37)
+constexpr int KS_K = 64;    // key block (attention.py:38-39)
+
+// ---------------------------------------------------------------- rounding
+__device__ __forceinline__ float bf16r(float x) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+}
+__device__ __forceinline__ float f16r(float x) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ uint16_t f16bits(float x) {
+    return __half_as_ushort(__float2half_rn(x));
+}
+__device__ __forceinline__ uint16_t bf16bits(float x) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+__device__ __forceinline__ float bf16_from_bits(uint16_t b) {
+    return __uint_as_float(((uint32_t)b) << 16);
+}
+
+template <typename T> struct DT;
+template <> struct DT<float> {
+    static constexpr int code = RESS_F32;
+    __device__ __forceinline__ static float load(const float *p, size_t i) { return p[i]; }
+    __device__ __forceinline__ static float round(float x) { return x; }
+    __device__ __forceinline__ static void store(float *p, size_t i, float v) { p[i] = v; }
+};
+template <> struct DT<__nv_bfloat16> {
+    static constexpr int code = RESS_BF16;
+    __device__ __forceinline__ static float load(const __nv_bfloat16 *p, size_t i) {
+        return __bfloat162float(p[i]);
+    }
+    __device__ __forceinline__ static float round(float x) { return bf16r(x); }
+    __device__ __forceinline__ static void store(__nv_bfloat16 *p, size_t i, float v) {
+        p[i] = __float2bfloat16_rn(v);
+    }
+};
+
+// torch clamp(min=m): (x < m) ? m : x -- keeps -0.0 and NaN.
+__device__ __forceinline__ float clamp_min(float x, float m) { return (x < m) ? m : x; }
+
+// exp(x): Cody-Waite two-word ln2 reduction, degree-7 Taylor polynomial in
+// Horner form with fma, exact scaling by 2^n.  Same operation sequence as
+// ress_expf in the oracle, so the two agree bit for bit.
+__device__ __forceinline__ float ress_expf(float x) {
+    if (x != x) return x;
+    if (x < -104.0f) return 0.0f;
+    if (x > 88.7f) return __int_as_float(0x7f800000);
+    const float log2e = 1.44269502162933349609375f;
+    const float ln2_hi = 0.693145751953125f;
+    const float ln2_lo = 1.428606765330187e-06f;
+    float n = rintf(__fmul_rn(x, log2e));
+    float r = __fmaf_rn(-n, ln2_hi, x);
+    r = __fmaf_rn(-n, ln2_lo, r);
+    float p = 1.98412698e-04f;
+    p = __fmaf_rn(p, r, 1.38888889e-03f);
+    p = __fmaf_rn(p, r, 8.33333377e-03f);
+    p = __fmaf_rn(p, r, 4.16666679e-02f);
+    p = __fmaf_rn(p, r, 1.66666672e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    int ni = (int)n;
+    if (ni >= -126) return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+    p = __fmul_rn(p, __int_as_float((ni + 100 + 127) << 23));
+    return __fmul_rn(p, __int_as_float((-100 + 127) << 23));
+}
+
+// Order-preserving uint32 key (fused_topm.py:51-56): -0 < +0.
+__device__ __forceinline__ uint32_t order_key(float x) {
+    uint32_t u = __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---------------------------------------------------------------- block helpers
+template <int NT>
+__device__ __forceinline__ int block_sum_int(int v, int *red) {
+    constexpr int NW = NT / 32;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    int t = 0;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) t += red[i];
+    return t;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_max_float(float v, float *red) {
+    constexpr int NW = NT / 32;
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = red[0];
+#pragma unroll
+    for (int i = 1; i < NW; ++i) t = fmaxf(t, red[i]);
+    return t;
+}
+
+// Exclusive prefix sum over the block in thread order; returns the prefix of
+// this thread and writes the block total to *total.
+template <int NT>
+__device__ __forceinline__ int block_excl_scan(int v, int *red, int *total) {
+    constexpr int NW = NT / 32;
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    int x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (l >= o) x += y;
+    }
+    __syncthreads();
+    if (l == 31) red[w] = x;
+    __syncthreads();
+    int base = 0, tot = 0;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        if (i < w) base += red[i];
+        tot += red[i];
+    }
+    *total = tot;
+    return base + x - v;
+}
+
+// Shared scratch for block_select_top_m.
+struct SelectScratch {
+    int hist[256];
+    int red[32];
+    int bin;
+    int remaining;
+};
+
+// Exact top-m over n entries held in shared memory (key[i], valid[i]),
+// ties to the lowest index; writes sel[i] in {0, 1}.  Each thread owns the
+// contiguous index range [tid*chunk, (tid+1)*chunk).  MSB-first radix
+// select with 8-bit digits finds the m-th largest valid key; entries above
+// it are taken, then the first (m - #above) equal entries in index order.
+// Semantics of fused_topm.py:67-80 (m clamped to [0, n_valid]).
+template <int NT>
+__device__ void block_select_top_m(const uint32_t *key, const uint8_t *valid, int n, int m,
+                                   uint8_t *sel, SelectScratch &sc) {
+    const int tid = threadIdx.x;
+    const int chunk = (n + NT - 1) / NT;
+    const int i0 = tid * chunk, i1 = min(n, i0 + chunk);
+    int nv = 0;
+    for (int i = i0; i < i1; ++i) nv += valid[i] ? 1 : 0;
+    int n_valid = block_sum_int<NT>(nv, sc.red);
+    if (m < 0) m = 0;
+    if (m >= n_valid || m == 0) {
+        bool all = (m > 0);
+        for (int i = i0; i < i1; ++i) sel[i] = (all && valid[i]) ? 1 : 0;
+        __syncthreads();
+        return;
+    }
+    uint32_t prefix = 0, pmask = 0;
+    int rem = m;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int b = tid; b < 256; b += NT) sc.hist[b] = 0;
+        __syncthreads();
+        for (int i = i0; i < i1; ++i) {
+            uint32_t k = key[i];
+            if (valid[i] && (k & pmask) == prefix) atomicAdd(&sc.hist[(k >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        // find the bin b with count(> b) < rem <= count(>= b), scanning from 255 down
+        if (tid < 32) {
+            // each lane owns 8 bins: lane l -> bins 255-8l .. 248-8l (descending)
+            int c[8], s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { c[j] = sc.hist[255 - 8 * tid - j]; s += c[j]; }
+            int x = s;
+            for (int o = 1; o < 32; o <<= 1) {
+                int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (tid >= o) x += y;
+            }
+            int before = x - s;  // count in bins above this lane's range
+            if (before < rem && rem <= x) {
+                int acc = before;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (acc < rem && rem <= acc + c[j]) {
+                        sc.bin = 255 - 8 * tid - j;
+                        sc.remaining = rem - acc;
+                    }
+                    acc += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        prefix |= ((uint32_t)sc.bin) << shift;
+        pmask |= 255u << shift;
+        rem = sc.remaining;
+        __syncthreads();
+    }
+    // prefix == threshold key; rem == number of equal entries to take
+    int eq = 0;
+    for (int i = i0; i < i1; ++i) eq += (valid[i] && key[i] == prefix) ? 1 : 0;
+    int tot;
+    int before = block_excl_scan<NT>(eq, sc.red, &tot);
+    for (int i = i0; i < i1; ++i) {
+        uint8_t s = 0;
+        if (valid[i]) {
+            uint32_t k = key[i];
+            if (k > prefix) s = 1;
+            else if (k == prefix) { s = (before < rem) ? 1 : 0; ++before; }
+        }
+        sel[i] = s;
+    }
+    __syncthreads();
+}
+
+}  // namespace ress

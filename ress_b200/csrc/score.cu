@@ -1,0 +1,511 @@
+// score.cu -- block-map scoring: window means, int8 quantisation, pooled
+// softmax, candidate renormalisation, baseline count and the HeSS budget.
+//
+// Reference functions restated (libary753/ReSS):
+//   predict_attention / block_mean_value   src/ress/models/attention.py:82-109
+//   attn_cond, n_cand, sink blocks          src/ress/models/attention.py:446-491
+//   compute_baseline_num_to_select          src/ress/models/attention.py:268-293
+//   adjust_attention_selection              src/ress/budget/_proportional.py:149-215
+//   run_block_sparse_kernel quantisation    src/ress/models/attention.py:226-233
+//   SpargeAttn per_block_int8 (+ patch)     external/patches/spargeattn.patch:32-42
+// The operation order matches oracle/ress_oracle.c; see that file's header
+// for the numeric contract.
+#include "common.cuh"
+
+namespace ress {
+
+// Full-layout token index of the p-th patch token (frame-major) and of the
+// s-th special token.
+__device__ __forceinline__ long long patch_tok(int p, int S, int HW) {
+    int f = p / HW;
+    return (long long)f * (HW + S) + S + (p - f * HW);
+}
+__device__ __forceinline__ long long special_tok(int s, int S, int HW) {
+    int f = s / S;
+    return (long long)f * (HW + S) + (s - f * S);
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T *src, float *dst);
+template <>
+__device__ __forceinline__ void load8<float>(const float *src, float *dst) {
+    float4 a = *reinterpret_cast<const float4 *>(src);
+    float4 b = *reinterpret_cast<const float4 *>(src + 4);
+    dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+    dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16 *src, float *dst) {
+    uint4 u = *reinterpret_cast<const uint4 *>(src);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        dst[2 * i] = __uint_as_float(w[i] << 16);
+        dst[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+
+constexpr int POOL_NT = 256;
+
+// Quantise a tile of fp16-valued floats (rows x 64, row stride 65) held in
+// shared memory: scale = amax/127, q = trunc(x/scale + 0.5*sign(x)).
+__device__ __forceinline__ void quant_tile(const float (*tile)[65], int rows, int8_t *dst,
+                                           float *scale_out, float *red) {
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < rows * 64; i += POOL_NT) amax = fmaxf(amax, fabsf(tile[i >> 6][i & 63]));
+    amax = block_max_float<POOL_NT>(amax, red);
+    float sc = __fdiv_rn(amax, 127.0f);
+    if (threadIdx.x == 0) *scale_out = sc;
+    // 8 consecutive codes per thread -> one 8-byte store
+    for (int i = threadIdx.x; i < rows * 8; i += POOL_NT) {
+        int r = i >> 3, c = (i & 7) * 8;
+        uint32_t w[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int8_t qv = 0;
+            if (sc != 0.0f) {
+                float v = __fdiv_rn(tile[r][c + j], sc);
+                v = __fadd_rn(v, v >= 0.0f ? 0.5f : -0.5f);
+                qv = (int8_t)truncf(v);
+            }
+            w[j >> 2] |= ((uint32_t)(uint8_t)qv) << ((j & 3) * 8);
+        }
+        *reinterpret_cast<uint2 *>(dst + (size_t)r * 64 + c) = make_uint2(w[0], w[1]);
+    }
+}
+
+// Pass over Q: pooled Q (128-token windows over patch tokens) and int8 Q.
+template <typename T>
+__global__ void __launch_bounds__(POOL_NT) pool_q_kernel(
+    const T *__restrict__ q, int H, int S, int HW, int Tp, long long sb, long long sh,
+    long long st, T *__restrict__ qbar, int8_t *__restrict__ q8, float *__restrict__ qscale) {
+    __shared__ float tile[KS_Q][65];
+    __shared__ float red[32];
+    const int qb = blockIdx.x, bh = blockIdx.y, nqb = gridDim.x;
+    const int b = bh / H, h = bh - b * H;
+    const T *base = q + b * sb + h * sh;
+    const int t0 = qb * KS_Q, cnt = min(KS_Q, Tp - t0);
+    for (int i = threadIdx.x; i < KS_Q * 8; i += POOL_NT) {
+        int r = i >> 3, c = (i & 7) * 8;
+        float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (r < cnt) load8<T>(base + patch_tok(t0 + r, S, HW) * st + c, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) tile[r][c + j] = v[j];
+    }
+    __syncthreads();
+    if (qbar != nullptr && threadIdx.x < HD) {
+        const int d = threadIdx.x;
+        float s = 0.0f;
+        for (int t = 0; t < cnt; ++t) s = __fadd_rn(s, tile[t][d]);
+        DT<T>::store(qbar, ((size_t)bh * nqb + qb) * HD + d, __fdiv_rn(s, (float)cnt));
+    }
+    if (q8 == nullptr) return;
+    __syncthreads();
+    for (int i = threadIdx.x; i < cnt * HD; i += POOL_NT) tile[i >> 6][i & 63] = f16r(tile[i >> 6][i & 63]);
+    __syncthreads();
+    quant_tile(tile, cnt, q8 + ((size_t)bh * Tp + t0) * HD, qscale + (size_t)bh * nqb + qb, red);
+}
+
+// Pass over K and V in key order: pooled K/V (64-token windows over patch
+// tokens), fp16 V, and per-block fp16 sums of K for the key mean.
+template <typename T>
+__global__ void __launch_bounds__(POOL_NT) pool_kv_kernel(
+    const T *__restrict__ k, const T *__restrict__ v, int H, int S, int HW, int Tp, int Tk,
+    long long sb, long long sh, long long st, T *__restrict__ kbar, T *__restrict__ vbar,
+    uint16_t *__restrict__ v16, float *__restrict__ kpart) {
+    __shared__ float kt[KS_K][65];
+    __shared__ float vt[KS_K][65];
+    const int kb = blockIdx.x, bh = blockIdx.y, nkb = gridDim.x;
+    const int b = bh / H, h = bh - b * H;
+    const int c0 = kb * KS_K, nvalid = min(KS_K, Tk - c0);
+    const int npatch = max(0, min(KS_K, Tp - c0));
+    const int nkp = (Tp + KS_K - 1) / KS_K;
+    for (int i = threadIdx.x; i < KS_K * 16; i += POOL_NT) {
+        int r = (i >> 3) & 63, c = (i & 7) * 8;
+        bool isv = i >= KS_K * 8;
+        float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (r < nvalid) {
+            int cc = c0 + r;
+            long long tok = cc < Tp ? patch_tok(cc, S, HW) : special_tok(cc - Tp, S, HW);
+            const T *src = (isv ? v : k) + b * sb + h * sh + tok * st + c;
+            load8<T>(src, x);
+        }
+        float(*dst)[65] = isv ? vt : kt;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[r][c + j] = x[j];
+    }
+    __syncthreads();
+    const int tid = threadIdx.x;
+    if (kbar != nullptr && kb < nkp && tid < 2 * HD) {
+        const int d = tid & 63;
+        const bool isv = tid >= HD;
+        float(*src)[65] = isv ? vt : kt;
+        float s = 0.0f;
+        for (int t = 0; t < npatch; ++t) s = __fadd_rn(s, src[t][d]);
+        DT<T>::store(isv ? vbar : kbar, ((size_t)bh * nkp + kb) * HD + d, __fdiv_rn(s, (float)npatch));
+    }
+    if (kpart != nullptr && tid >= 2 * HD && tid < 3 * HD) {
+        const int d = tid - 2 * HD;
+        float s = 0.0f;
+        for (int t = 0; t < nvalid; ++t) s = __fadd_rn(s, f16r(kt[t][d]));
+        kpart[((size_t)bh * nkb + kb) * HD + d] = s;
+    }
+    if (v16 != nullptr) {
+        for (int i = tid; i < nvalid * 8; i += POOL_NT) {
+            int r = i >> 3, c = (i & 7) * 8;
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                w[j] = (uint32_t)f16bits(vt[r][c + 2 * j]) | ((uint32_t)f16bits(vt[r][c + 2 * j + 1]) << 16);
+            *reinterpret_cast<uint4 *>(v16 + ((size_t)bh * Tk + c0 + r) * HD + c) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// km = fp16((sum over key blocks of the block sums) / Tk), sequential.
+__global__ void key_mean_kernel(const float *__restrict__ kpart, int nkb, int Tk, float *__restrict__ km) {
+    const int bh = blockIdx.x, d = threadIdx.x;
+    float s = 0.0f;
+    for (int j = 0; j < nkb; ++j) s = __fadd_rn(s, kpart[((size_t)bh * nkb + j) * HD + d]);
+    km[(size_t)bh * HD + d] = f16r(__fdiv_rn(s, (float)Tk));
+}
+
+// Second pass over K: int8 of fp16(fp16(k) - km) per 64-key block.
+template <typename T>
+__global__ void __launch_bounds__(POOL_NT) kquant_kernel(
+    const T *__restrict__ k, int H, int S, int HW, int Tp, int Tk, long long sb, long long sh,
+    long long st, const float *__restrict__ km, int8_t *__restrict__ k8, float *__restrict__ kscale) {
+    __shared__ float kt[KS_K][65];
+    __shared__ float red[32];
+    const int kb = blockIdx.x, bh = blockIdx.y, nkb = gridDim.x;
+    const int b = bh / H, h = bh - b * H;
+    const int c0 = kb * KS_K, nvalid = min(KS_K, Tk - c0);
+    for (int i = threadIdx.x; i < KS_K * 8; i += POOL_NT) {
+        int r = i >> 3, c = (i & 7) * 8;
+        float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (r < nvalid) {
+            int cc = c0 + r;
+            long long tok = cc < Tp ? patch_tok(cc, S, HW) : special_tok(cc - Tp, S, HW);
+            load8<T>(k + b * sb + h * sh + tok * st + c, x);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) x[j] = f16r(__fsub_rn(f16r(x[j]), km[(size_t)bh * HD + c + j]));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) kt[r][c + j] = x[j];
+    }
+    __syncthreads();
+    quant_tile(kt, nvalid, k8 + ((size_t)bh * Tk + c0) * HD, kscale + (size_t)bh * nkb + kb, red);
+}
+
+// ------------------------------------------------------------------ predict
+constexpr int PRED_NT = 256;
+
+// One CTA handles `rows` consecutive q-blocks of one head (rows <= 8, one
+// warp per row for the row-wise steps).
+template <typename T>
+__global__ void __launch_bounds__(PRED_NT) predict_kernel(
+    const T *__restrict__ qbar, const T *__restrict__ kbar, int nq, int nkp, int n_cand,
+    int rows_per_cta, float scale, T *__restrict__ attn_full, T *__restrict__ attn_cond) {
+    extern __shared__ float smem[];
+    float *qs = smem;                               // rows x 64
+    float *sc = qs + 8 * HD;                        // rows x nkp
+    __shared__ float rowsum[8];
+    const int bh = blockIdx.y;
+    const int q0 = blockIdx.x * rows_per_cta;
+    const int nr = min(rows_per_cta, nq - q0);
+    const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+    for (int i = tid; i < nr * HD; i += PRED_NT)
+        qs[i] = DT<T>::load(qbar, ((size_t)bh * nq + q0) * HD + i);
+    __syncthreads();
+    for (int j = tid; j < nkp; j += PRED_NT) {
+        float kv[HD];
+        const T *kp = kbar + ((size_t)bh * nkp + j) * HD;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) kv[d] = DT<T>::load(kp, d);
+        for (int r = 0; r < nr; ++r) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int d = 0; d < HD; ++d) acc = __fmaf_rn(qs[r * HD + d], kv[d], acc);
+            acc = DT<T>::round(acc);
+            sc[(size_t)r * nkp + j] = DT<T>::round(__fmul_rn(acc, scale));
+        }
+    }
+    __syncthreads();
+    // softmax per row: warp w handles row w
+    if (w < nr) {
+        float *x = sc + (size_t)w * nkp;
+        float m = -__int_as_float(0x7f800000);
+        for (int j = l; j < nkp; j += 32) m = fmaxf(m, x[j]);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        for (int j = l; j < nkp; j += 32) x[j] = ress_expf(__fsub_rn(x[j], m));
+        __syncwarp();
+        if (l == 0) {
+            float s = 0.0f;
+            for (int j = 0; j < nkp; ++j) s = __fadd_rn(s, x[j]);
+            rowsum[w] = s;
+        }
+        __syncwarp();
+        const float s = rowsum[w];
+        const size_t ob = ((size_t)bh * nq + q0 + w) * nkp;
+        for (int j = l; j < nkp; j += 32) {
+            float a = DT<T>::round(__fdiv_rn(x[j], s));
+            x[j] = a;
+            if (attn_full) DT<T>::store(attn_full, ob + j, a);
+        }
+        __syncwarp();
+        if (l == 0) {
+            float s2 = 0.0f;
+            for (int j = 0; j < n_cand; ++j) s2 = __fadd_rn(s2, x[j]);
+            rowsum[w] = clamp_min(DT<T>::round(s2), DT<T>::round(1e-6f));
+        }
+        __syncwarp();
+        const float s2 = rowsum[w];
+        const size_t cb = ((size_t)bh * nq + q0 + w) * n_cand;
+        for (int j = l; j < n_cand; j += 32) {
+            float c = DT<T>::round(__fdiv_rn(x[j], s2));
+            x[j] = c;
+            if (attn_cond) DT<T>::store(attn_cond, cb + j, c);
+        }
+    }
+}
+
+// CDF / ratio baseline from a pooled candidate map (attention.py:268-293).
+// One CTA per row: bitonic sort (descending) in shared memory, then the
+// sequential running sum of the sorted values (fp32 accumulator rounded to
+// bf16 per prefix for bf16 maps; fp64 accumulator rounded to fp32 per prefix
+// for fp32 maps, as torch's CPU cumsum) counted against cdf_value.
+template <typename T>
+__global__ void __launch_bounds__(PRED_NT) baseline_kernel(const T *__restrict__ cond, int n, int use_cdf,
+                                                           float cdf_value, int topk, int sort_n,
+                                                           int32_t *__restrict__ baseline) {
+    extern __shared__ float srt[];
+    __shared__ int cnt_out;
+    const int row = blockIdx.x, tid = threadIdx.x;
+    int count = topk;
+    if (use_cdf) {
+        for (int i = tid; i < sort_n; i += PRED_NT)
+            srt[i] = i < n ? DT<T>::load(cond, (size_t)row * n + i) : -__int_as_float(0x7f800000);
+        __syncthreads();
+        for (int kk = 2; kk <= sort_n; kk <<= 1) {
+            for (int jj = kk >> 1; jj > 0; jj >>= 1) {
+                for (int i = tid; i < sort_n; i += PRED_NT) {
+                    int ixj = i ^ jj;
+                    if (ixj > i) {
+                        float a = srt[i], c = srt[ixj];
+                        bool desc = (i & kk) == 0;
+                        if (desc ? (a < c) : (a > c)) { srt[i] = c; srt[ixj] = a; }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        if (tid == 0) {
+            int c = 0;
+            if (DT<T>::code == RESS_BF16) {
+                float acc = 0.0f;
+                for (; c < n; ++c) {
+                    acc = __fadd_rn(acc, srt[c]);
+                    if (!(bf16r(acc) <= cdf_value)) break;
+                }
+            } else {
+                double acc = 0.0;
+                for (; c < n; ++c) {
+                    acc = __dadd_rn(acc, (double)srt[c]);
+                    if (!(__double2float_rn(acc) <= cdf_value)) break;
+                }
+            }
+            cnt_out = c;
+        }
+        __syncthreads();
+        count = (topk >= 0 && cnt_out < topk) ? topk : cnt_out;
+    }
+    if (tid == 0) baseline[row] = count;
+}
+
+// ------------------------------------------------------------------ HeSS
+// One warp per (b, q) column; lane h holds head h (H <= 32).  Sums over
+// heads are sequential in head order, computed redundantly by every lane.
+__global__ void hess_kernel(const int32_t *__restrict__ base, const float *__restrict__ snorm, int B,
+                            int H, int nq, int max_val, float one_minus_beta, float beta,
+                            int max_iters, int min_clamp, int32_t *__restrict__ nts,
+                            int32_t *__restrict__ status) {
+    const int col = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int l = threadIdx.x & 31;
+    if (col >= B * nq) return;
+    const int b = col / nq, q = col - b * nq;
+    const bool act = l < H;
+    const float fmax_ = (float)max_val;
+    int n = act ? base[((size_t)b * H + l) * nq + q] : 0;
+    long long total = 0;
+    for (int h = 0; h < H; ++h) total += __shfl_sync(0xffffffffu, n, h);
+    float ideal = act ? __fmul_rn(snorm[l], (float)total) : 0.0f;
+    float adj = __fadd_rn(__fmul_rn(one_minus_beta, (float)n), __fmul_rn(beta, ideal));
+    int it = 0;
+    for (; it < max_iters; ++it) {
+        float ex = act ? clamp_min(__fsub_rn(adj, fmax_), 0.0f) : 0.0f;
+        bool fin = isfinite(ex);
+        bool any = ex > 0.0f;
+        if (!__all_sync(0xffffffffu, fin) || !__any_sync(0xffffffffu, any)) break;
+        float tot = 0.0f;
+        for (int h = 0; h < H; ++h) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, ex, h));
+        adj = (adj > fmax_) ? fmax_ : adj;
+        float wgt = (act && adj < fmax_) ? adj : 0.0f;
+        float ws = 0.0f;
+        for (int h = 0; h < H; ++h) ws = __fadd_rn(ws, __shfl_sync(0xffffffffu, wgt, h));
+        float den = __fadd_rn(ws, 1e-9f);
+        adj = __fadd_rn(adj, __fmul_rn(__fdiv_rn(wgt, den), tot));
+    }
+    if (it == max_iters && l == 0) atomicOr(status, RESS_STATUS_HESS_NO_CONVERGENCE);
+    if (act) {
+        float a = (adj > fmax_) ? fmax_ : adj;
+        int v = (int)floorf(a);
+        nts[((size_t)b * H + l) * nq + q] = v < min_clamp ? min_clamp : v;
+    }
+}
+
+// ------------------------------------------------------------------ launchers
+template <typename T>
+static int pool_quant_q_t(const void *q, int B, int H, int frames, int S, int HW, long long sb, long long sh,
+                          long long st, void *qbar, int8_t *q8, float *qscale, cudaStream_t s) {
+    const int Tp = frames * HW, BH = B * H, nqb = (Tp + KS_Q - 1) / KS_Q;
+    pool_q_kernel<T><<<dim3(nqb, BH), POOL_NT, 0, s>>>((const T *)q, H, S, HW, Tp, sb, sh, st, (T *)qbar, q8,
+                                                      qscale);
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}
+
+template <typename T>
+static int pool_quant_kv_t(const void *k, const void *v, int B, int H, int frames, int S, int HW, long long sb,
+                           long long sh, long long st, void *kbar, void *vbar, int8_t *k8, float *kscale,
+                           uint16_t *v16, float *km, void *ws, cudaStream_t s) {
+    const int Tp = frames * HW, Tk = Tp + frames * S, BH = B * H;
+    const int nkb = (Tk + KS_K - 1) / KS_K;
+    float *kpart = reinterpret_cast<float *>(ws);
+    pool_kv_kernel<T><<<dim3(nkb, BH), POOL_NT, 0, s>>>((const T *)k, (const T *)v, H, S, HW, Tp, Tk, sb, sh, st,
+                                                       (T *)kbar, (T *)vbar, v16, k8 ? kpart : nullptr);
+    if (k8 != nullptr) {
+        key_mean_kernel<<<BH, HD, 0, s>>>(kpart, nkb, Tk, km);
+        kquant_kernel<T><<<dim3(nkb, BH), POOL_NT, 0, s>>>((const T *)k, H, S, HW, Tp, Tk, sb, sh, st, km, k8,
+                                                          kscale);
+    }
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}
+
+template <typename T>
+static int predict_t(const void *qbar, const void *kbar, int BH, int nq, int nkp, int n_cand, void *attn_full,
+                     void *attn_cond, cudaStream_t s) {
+    int rows = 8;
+    auto smem = [&](int r) { return (size_t)(8 * HD + (size_t)r * nkp) * sizeof(float); };
+    while (rows > 1 && smem(rows) > 160 * 1024) rows >>= 1;
+    if (smem(rows) > 220 * 1024) return RESS_E_SHAPE;
+    size_t sm = smem(rows);
+    auto kern = predict_kernel<T>;
+    if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    dim3 grid((nq + rows - 1) / rows, BH);
+    kern<<<grid, PRED_NT, sm, s>>>((const T *)qbar, (const T *)kbar, nq, nkp, n_cand, rows, 0.125f, (T *)attn_full,
+                                   (T *)attn_cond);
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}
+
+template <typename T>
+static int baseline_t(const void *cond, int rows, int n, int use_cdf, float cdf_value, int topk, int32_t *out,
+                      cudaStream_t s) {
+    int sort_n = 1;
+    while (sort_n < n) sort_n <<= 1;
+    if (!use_cdf) sort_n = 0;
+    size_t sm = (size_t)sort_n * sizeof(float);
+    auto kern = baseline_kernel<T>;
+    if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    kern<<<rows, PRED_NT, sm, s>>>((const T *)cond, n, use_cdf, cdf_value, topk, sort_n, out);
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}
+
+}  // namespace ress
+
+using namespace ress;
+
+static int layout_ok(const void *a, int B, int H, int frames, int special, int hw, long long sb, long long sh,
+                     long long st) {
+    if (!a || B <= 0 || H <= 0 || frames <= 0 || special < 0 || hw <= 0) return 0;
+    if ((uintptr_t)a & 15) return 0;
+    if ((st & 7) || (sh & 7) || (sb & 7)) return 0;  // 16-byte vector loads (8 bf16 / 4+4 fp32)
+    return 1;
+}
+
+extern "C" int ress_pool_quant_q(const void *q, int dtype, int B, int H, int frames, int special, int hw,
+                                 long long sb, long long sh, long long st, void *qbar, int8_t *q8, float *qscale,
+                                 ress_stream_t stream) {
+    if (!layout_ok(q, B, H, frames, special, hw, sb, sh, st)) return RESS_E_ARG;
+    if ((q8 == nullptr) != (qscale == nullptr) || (!qbar && !q8)) return RESS_E_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dtype == RESS_F32) return pool_quant_q_t<float>(q, B, H, frames, special, hw, sb, sh, st, qbar, q8, qscale, s);
+    if (dtype == RESS_BF16)
+        return pool_quant_q_t<__nv_bfloat16>(q, B, H, frames, special, hw, sb, sh, st, qbar, q8, qscale, s);
+    return RESS_E_DTYPE;
+}
+
+extern "C" int ress_pool_quant_kv(const void *k, const void *v, int dtype, int B, int H, int frames, int special,
+                                  int hw, long long sb, long long sh, long long st, void *kbar, void *vbar,
+                                  int8_t *k8, float *kscale, uint16_t *v16, float *km, void *workspace,
+                                  ress_stream_t stream) {
+    if (!layout_ok(k, B, H, frames, special, hw, sb, sh, st) || !layout_ok(v, B, H, frames, special, hw, sb, sh, st))
+        return RESS_E_ARG;
+    if ((kbar == nullptr) != (vbar == nullptr)) return RESS_E_ARG;
+    const bool quant = k8 != nullptr;
+    if (quant && (!kscale || !v16 || !km || !workspace)) return RESS_E_ARG;
+    if (!quant && (kscale || km)) return RESS_E_ARG;
+    if (!kbar && !quant && !v16) return RESS_E_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dtype == RESS_F32)
+        return pool_quant_kv_t<float>(k, v, B, H, frames, special, hw, sb, sh, st, kbar, vbar, k8, kscale, v16, km,
+                                      workspace, s);
+    if (dtype == RESS_BF16)
+        return pool_quant_kv_t<__nv_bfloat16>(k, v, B, H, frames, special, hw, sb, sh, st, kbar, vbar, k8, kscale,
+                                              v16, km, workspace, s);
+    return RESS_E_DTYPE;
+}
+
+extern "C" int ress_score_quant(const void *q, const void *k, const void *v, int dtype, int B, int H, int frames,
+                                int special, int hw, long long sb, long long sh, long long st, void *qbar,
+                                void *kbar, void *vbar, int8_t *q8, float *qscale, int8_t *k8, float *kscale,
+                                uint16_t *v16, float *km, void *workspace, ress_stream_t stream) {
+    if ((qbar == nullptr) != (kbar == nullptr)) return RESS_E_ARG;
+    if ((q8 == nullptr) != (k8 == nullptr)) return RESS_E_ARG;
+    int rc = ress_pool_quant_q(q, dtype, B, H, frames, special, hw, sb, sh, st, qbar, q8, qscale, stream);
+    if (rc != RESS_OK) return rc;
+    return ress_pool_quant_kv(k, v, dtype, B, H, frames, special, hw, sb, sh, st, kbar, vbar, k8, kscale, v16, km,
+                              workspace, stream);
+}
+
+extern "C" int ress_predict(int dtype, const void *qbar, const void *kbar, int BH, int nq, int nkp, int n_cand,
+                            void *attn_full, void *attn_cond, ress_stream_t stream) {
+    if (!qbar || !kbar || BH <= 0 || nq <= 0 || nkp <= 0 || n_cand <= 0 || n_cand > nkp) return RESS_E_ARG;
+    if (!attn_full && !attn_cond) return RESS_E_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dtype == RESS_F32) return predict_t<float>(qbar, kbar, BH, nq, nkp, n_cand, attn_full, attn_cond, s);
+    if (dtype == RESS_BF16) return predict_t<__nv_bfloat16>(qbar, kbar, BH, nq, nkp, n_cand, attn_full, attn_cond, s);
+    return RESS_E_DTYPE;
+}
+
+extern "C" int ress_baseline(int dtype, const void *attn_cond, int rows, int n, int use_cdf, float cdf_value,
+                             int topk, int32_t *baseline, ress_stream_t stream) {
+    if (!attn_cond || !baseline || rows < 0 || n <= 0) return RESS_E_ARG;
+    if (!use_cdf && topk < 0) return RESS_E_ARG;
+    if (use_cdf && n > 16384) return RESS_E_SHAPE;
+    if (rows == 0) return RESS_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dtype == RESS_F32) return baseline_t<float>(attn_cond, rows, n, use_cdf, cdf_value, topk, baseline, s);
+    if (dtype == RESS_BF16) return baseline_t<__nv_bfloat16>(attn_cond, rows, n, use_cdf, cdf_value, topk, baseline, s);
+    return RESS_E_DTYPE;
+}
+
+extern "C" int ress_hess_adjust(const int32_t *base, const float *scores_norm, int B, int H, int nq,
+                                int max_val, float one_minus_beta, float beta, int max_iters,
+                                int min_clamp, int32_t *nts, int32_t *status, ress_stream_t stream) {
+    if (!base || !scores_norm || !nts || !status || B <= 0 || H <= 0 || H > 32 || nq <= 0 ||
+        max_val <= 0 || max_iters <= 0)
+        return RESS_E_ARG;
+    const int cols = B * nq, wpb = 8;
+    hess_kernel<<<(cols + wpb - 1) / wpb, 32 * wpb, 0, (cudaStream_t)stream>>>(
+        base, scores_norm, B, H, nq, max_val, one_minus_beta, beta, max_iters, min_clamp, nts, status);
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}

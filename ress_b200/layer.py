@@ -1,0 +1,187 @@
+"""One sparse global-attention layer on the GPU, end to end.
+
+This is the body of the reference's ``ress_attention_forward`` after the
+Q/K/V projection (src/ress/models/attention.py:404-659), chained from the
+library's kernels with no host synchronisation:
+
+  1. ress_pool_quant_q / _kv   pooled means (a.3, a.4) and int8 Q/K, fp16 V
+                               (a.12) in one read of Q, K and V each
+  2. ress_predict              pooled softmax + candidate renormalisation (a.3, a.5)
+  3. ress_baseline             CDF / ratio budget (a.6)
+  4. ress_hess_adjust          HeSS per-head re-allocation (a.7), when the
+                               budget is HeSS
+  5. ress_restore_swap         ReSS ordering -> keep lists (a.8-a.11), or
+     ress_select_prob          probability ordering -> keep lists (a.11)
+  6. ress_sparse_attn          tcgen05 block-sparse attention (a.12), written
+                               straight into the full token layout
+  7. torch SDPA                the special-token queries attend densely to all
+                               keys (a.2), on a side stream
+
+The input tensors are the layer's q, k, v in the full token layout
+(B, H, frames * (special + hw), 64): the patch/special split of the reference
+(models/tokens.py) is folded into the kernels' index arithmetic, and the
+output lands in the same layout, which is what combine_special_and_patch
+(models/qkv.py:71-81) would have produced.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels as K
+
+MIN_NUM_TO_SELECT = 2  # attention.py:40
+
+
+@dataclass
+class BudgetSpec:
+    """How many blocks each (head, q-block) keeps (budget/hess.py,
+    budget/uniform.py).  kind: "uniform" or "hess"."""
+
+    kind: str
+    sparse_ratio: float | None = None
+    cdf_threshold: float | None = None
+    beta: float = 1.0
+    scores_norm: torch.Tensor | None = None  # (H,) for "hess"
+
+
+@dataclass
+class OrderSpec:
+    """Which blocks fill the budget.  kind: "probability", "restore_swap" or
+    "random"."""
+
+    kind: str = "probability"
+    M: torch.Tensor | None = None  # (H, 64, 64) fp32, restore_swap
+    n_iters: int = 5
+    track_best: bool = True
+    restore_frac: float = 0.5
+    decay: float = 0.5
+
+
+@dataclass
+class LayerResult:
+    out: torch.Tensor                  # (B, H, N*P, 64) fp32, full token layout
+    layout: K.Layout
+    lists: torch.Tensor                # (B*H*nq, width) int32 keep lists
+    counts: torch.Tensor               # (B*H*nq,) int32
+    nts: torch.Tensor                  # (B, H, nq) int32 budgets
+    attn_full: torch.Tensor | None = None
+    attn_cond: torch.Tensor | None = None
+    vbar: torch.Tensor | None = None
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def width(self) -> int:
+        return self.layout.n_cand + self.layout.sink_blocks
+
+    def sparsity(self) -> float:
+        """1 - mean(final_map), sinks counted (attention.py:242).  Synchronises."""
+        rows = self.counts.numel()
+        return 1.0 - float(self.counts.sum().item()) / float(rows * self.width)
+
+    def final_map(self) -> torch.Tensor:
+        """Dense (B, H, nq, width) bool block map (API compatibility only)."""
+        L = self.layout
+        m = K.lists_to_map(self.lists, self.counts, self.width)
+        return m.view(L.B, L.H, L.nq, self.width)
+
+
+_random_gens = {}
+
+
+def _random_gen(device):
+    """One generator per device for block_criterion="random", seeded once
+    (attention.py:177-196)."""
+    g = _random_gens.get(device)
+    if g is None:
+        g = torch.Generator(device=device).manual_seed(20260826)
+        _random_gens[device] = g
+    return g
+
+
+def special_attention(q, k, v, L: K.Layout):
+    """Dense SDPA of the special-token queries over all keys (attention.py:
+    404-409; the key order does not change a softmax)."""
+    if L.special == 0:
+        return None
+    B, H = L.B, L.H
+    qs = q.view(B, H, L.frames, L.special + L.hw, 64)[:, :, :, : L.special].reshape(B, H, L.Ts, 64)
+    return F.scaled_dot_product_attention(qs, k, v)
+
+
+def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSpec, *,
+                 num_to_select: torch.Tensor | None = None, budget_fn=None, keep_pooled: bool = False,
+                 lead_blocks: int = 0, out: torch.Tensor | None = None) -> LayerResult:
+    """Run one sparse global-attention layer.  q, k, v: (B, H, N*P, 64) CUDA,
+    float32 or bfloat16.  Exactly one of ``budget``, ``num_to_select`` (a
+    (B, H, nq) tensor) or ``budget_fn`` (callable(attn_cond) -> (B, H, nq))
+    decides the per-row block count."""
+    dev = q.device
+    if k.stride() != v.stride():
+        v = v.contiguous()
+        k = k.contiguous()
+    B, H = L.B, L.H
+    n_cand = L.n_cand
+    ws = K.workspace(dev, B * H, L.Tp, L.Tk, n_cand)
+    main = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        x_special = special_attention(q, k, v, L)
+    for t in (q, k, v):
+        t.record_stream(side)
+
+    qbar, q8, qs = K.pool_quant_q(q, L)
+    kbar, vbar, k8, ks, v16, km = K.pool_quant_kv(k, v, L, ws=ws)
+    need_full = order.kind == "restore_swap" or keep_pooled
+    attn_full, attn_cond = K.predict(qbar, kbar, n_cand, full=need_full, cond=True)
+    min_sel = min(MIN_NUM_TO_SELECT, n_cand)
+    if num_to_select is not None:
+        nts = num_to_select.to(device=dev, dtype=torch.int32).reshape(B, H, L.nq).clamp(min=min_sel)
+    elif budget is not None:
+        base = K.baseline(attn_cond, budget.sparse_ratio, budget.cdf_threshold).view(B, H, L.nq)
+        if budget.kind == "hess":
+            nts = K.hess_adjust(base, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
+        else:
+            nts = base.clamp(min=min_sel)
+    elif budget_fn is not None:
+        nts = budget_fn(attn_cond.view(B, H, L.nq, n_cand))
+        nts = nts.to(device=dev, dtype=torch.int32).reshape(B, H, L.nq).clamp(min=min_sel)
+    else:
+        raise AssertionError("num_to_select (or budget_fn) required unless dense=True")
+
+    if order.kind == "restore_swap":
+        r = K.restore_swap(attn_full, vbar, order.M, nts.view(-1), n_cand, n_iters=order.n_iters,
+                           track_best=order.track_best, restore_frac=order.restore_frac, decay=order.decay,
+                           sink_blocks=L.sink_blocks, lead_blocks=lead_blocks, ws=ws)
+    elif order.kind == "probability":
+        r = K.select_prob(attn_cond, nts.view(-1), sink_blocks=L.sink_blocks, lead_blocks=lead_blocks)
+    elif order.kind == "random":
+        key = torch.rand(attn_cond.shape, device=dev, dtype=torch.float32, generator=_random_gen(dev))
+        keep = K.top_m_mask(key, nts.view(-1)).view(-1, n_cand)
+        full_map = torch.cat([keep, torch.ones(keep.shape[0], L.sink_blocks, dtype=torch.bool, device=dev)], -1)
+        if lead_blocks:
+            full_map[:, :lead_blocks] = True
+        lists, counts = K.map_to_lists(full_map)
+        r = dict(lists=lists, counts=counts)
+    else:
+        raise ValueError(order.kind)
+
+    if out is None:
+        out = torch.empty(B, H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=dev)
+    K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L)
+    main.wait_stream(side)
+    if x_special is not None:
+        x_special.record_stream(main)
+        view = out.view(B, H, L.frames, L.special + L.hw, 64)
+        view[:, :, :, : L.special] = x_special.view(B, H, L.frames, L.special, 64).float()
+    return LayerResult(out=out, layout=L, lists=r["lists"], counts=r["counts"], nts=nts,
+                       attn_full=attn_full, attn_cond=attn_cond, vbar=vbar)
+
+
+def dense_layer(q, k, v, L: K.Layout) -> torch.Tensor:
+    """The dense=True branch (attention.py:484-486): exact SDPA, torch."""
+    return F.scaled_dot_product_attention(q, k, v)
