@@ -1,0 +1,429 @@
+"""Benchmark of the ReSS/HeSS sparse global-attention layer on B200.
+
+Workload: one VGGT global-attention layer at 32
+frames x (5 special + 37*37 patch) tokens = 43,968 tokens, 16 heads x 64,
+bf16, synthetic clustered Q/K/V; apply_ress(sparse_ratio=0.5, n_iters=5)
+with a HeSS budget from a log-normal (3, 24, 16) Fisher table mixed at
+lambda = 0.5.  One step = the whole layer after the Q/K/V projection:
+scoring + quantisation, budget, restore-swap selection, tcgen05 sparse
+attention, dense special-token queries, output in the full token layout.
+
+Metric: views of the global layer processed per second (32 views per step;
+the layer ms is reported beside it).  With --gpus N (torchrun) the 16 heads
+are split across the N GPUs (strong scaling); HeSS needs the baseline counts
+of all heads per q-block, which are all-gathered with NCCL.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ress|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_FRAMES = 32
+SPARSE_RATIO = 0.5
+CDF = 0.97
+METRIC = "global-attn layer throughput, VGGT cfg2 (32 views, 43,968 tokens, 16x64 heads, apply_ress sr=0.5)"
+UNIT = "views/s"
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ress", choices=["ress", "reference"])
+    ap.add_argument("--frames", type=int, default=N_FRAMES)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-attn", action="store_true", help="one small layer, for ncu")
+    return ap.parse_args()
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        else:
+            self.lines = []
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _setup(frames, world, rank, device):
+    from ress_b200 import kernels as K
+    from ress_b200 import layer as LY
+    from ress_b200 import synth
+
+    shape = synth.LayerShape(n_frames=frames)
+    q, k, v = synth.layer_qkv(shape, seed=0, dtype=torch.bfloat16, device=device)
+    H = shape.n_heads
+    if H % world:
+        raise SystemExit(f"{H} heads do not split over {world} GPUs")
+    hl = H // world
+    h0 = rank * hl
+    q, k, v = (t[:, h0:h0 + hl].contiguous() for t in (q, k, v))
+    L = K.Layout(1, hl, shape.n_frames, shape.n_special, shape.hw)
+    M = synth.metric_from_weight(synth.out_proj_weight(), H)[h0:h0 + hl].to(device)
+    # HessBudget tables: row 0 (W_Q) of two log-normal (3, 24, 16) tables, lambda = 0.5, layer 0
+    cam, pcd = synth.fisher_table(seed=1)[0], synth.fisher_table(seed=3)[0]
+    cam = cam / cam.sum(-1, keepdim=True)
+    pcd = pcd / pcd.sum(-1, keepdim=True)
+    comb = 0.5 * cam + 0.5 * pcd
+    head_scores = (comb / comb.sum(-1, keepdim=True))[0]
+    sn = K.scores_norm(head_scores).to(device)
+    shard = None
+    if world > 1:
+        import torch.distributed as dist
+
+        def gather(base):
+            out = torch.empty(world * base.numel(), dtype=base.dtype, device=base.device)
+            dist.all_gather_into_tensor(out, base.contiguous().view(-1))
+            B, Hl, nq = base.shape
+            return out.view(world, B, Hl, nq).permute(1, 0, 2, 3).reshape(B, world * Hl, nq).contiguous()
+
+        shard = LY.HeadShard(h0=h0, h_total=H, gather=gather)
+    budget = LY.BudgetSpec("hess", sparse_ratio=SPARSE_RATIO, cdf_threshold=None, scores_norm=sn)
+    budget_hess = LY.BudgetSpec("hess", sparse_ratio=SPARSE_RATIO, cdf_threshold=CDF, scores_norm=sn)
+    order = LY.OrderSpec("restore_swap", M=M, n_iters=5, track_best=True)
+    order_prob = LY.OrderSpec("probability")
+    return dict(shape=shape, q=q, k=k, v=v, L=L, budget=budget, budget_hess=budget_hess, order=order,
+                order_prob=order_prob, shard=shard, h0=h0, hl=hl)
+
+
+def _attn_flops(lists, counts, L):
+    """Kept-block FLOPs: 4 * q_rows * k_rows * 64 per (row, kept block)."""
+    rows = counts.numel()
+    nq = L.nq
+    qb = torch.arange(rows, device=counts.device) % nq
+    q_rows = (L.Tp - qb * 128).clamp(max=128).to(torch.float64)
+    ar = torch.arange(lists.shape[1], device=lists.device)
+    valid = ar.unsqueeze(0) < counts.unsqueeze(1)
+    k_rows = (L.Tk - lists.to(torch.int64) * 64).clamp(min=0, max=64).to(torch.float64)
+    k_sum = torch.where(valid, k_rows, torch.zeros_like(k_rows)).sum(1)
+    return float((4.0 * 64.0 * q_rows * k_sum).sum().item())
+
+
+def _time_region(fn, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def _cpu_baseline(S, samples_attn=8):
+    """The oracle (C, OpenMP over all host threads) on one cfg2 layer:
+    scoring + budget + restore-swap on the full layer, attention on a sample
+    of q-block rows extrapolated to the layer."""
+    import oracle
+    from ress_b200 import synth
+
+    shape = S["shape"]
+    q, k, v = (t.cpu() for t in (S["q"], S["k"], S["v"]))
+    qp, _ = synth.split_tokens(q, shape)
+    kp, ks = synth.split_tokens(k, shape)
+    vp, vs = synth.split_tokens(v, shape)
+    M = S["order"].M.cpu()
+    hs = S["budget"].scores_norm.cpu()
+    t0 = time.perf_counter()
+    o = oracle.layer_select(qp, kp, vp, ks.shape[-2], M, head_scores=hs, mode="ress", sparse_ratio=SPARSE_RATIO)
+    key = torch.cat([kp, ks], dim=-2)
+    val = torch.cat([vp, vs], dim=-2)
+    q8, qs, k8, ksc, km = oracle.quantize_qk(qp, key)
+    t1 = time.perf_counter()
+    H = qp.shape[1]
+    nq = o["nts"].shape[-1]
+    g = torch.Generator().manual_seed(0)
+    samp = [(int(torch.randint(0, H, (1,), generator=g)), int(torch.randint(0, nq, (1,), generator=g)))
+            for _ in range(samples_attn)]
+    v16 = val.reshape(H, -1, 64).to(torch.float16)
+    t2 = time.perf_counter()
+    oracle.sparse_attn_rows(q8, qs, k8, ksc, v16, o["lists"].view(H, nq, -1), o["counts"].view(H, nq), samp)
+    t3 = time.perf_counter()
+    per_layer = (t1 - t0) + (t3 - t2) * (H * nq) / samples_attn
+    return {"value": shape.n_frames / per_layer, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": (f"oracle scoring+quant+HeSS+restore-swap on the full cfg2 layer ({t1 - t0:.2f} s) + fp64 "
+                       f"attention on {samples_attn} of {H * nq} (head, q-block) rows ({t3 - t2:.2f} s), "
+                       f"extrapolated to one layer ({per_layer:.1f} s)")}
+
+
+def run_reference(args):
+    """--impl reference: the CPU path of the reference restated in the oracle,
+    on the host cores; rank 0 only."""
+    ws, rank, local = _dist()
+    if rank != 0:
+        return
+    device = "cuda" if torch.cuda.is_available() else "cpu"
+    S = _setup(args.frames, 1, 0, device)
+    steps = max(1, min(args.steps, 2))
+    vals = []
+    cb = None
+    for i in range(min(args.warmup, 1) + steps):
+        cb = _cpu_baseline(S, samples_attn=4)
+        if i >= min(args.warmup, 1):
+            vals.append(cb["value"])
+    value = sorted(vals)[len(vals) // 2]
+    cb["value"] = value
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": steps, "warmup": min(args.warmup, 1), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"cfg2 single global layer, {args.frames} views", "sparse_ratio": SPARSE_RATIO,
+                       "n_iters": 5, "note": "the reference's CPU path as restated by the oracle; steps capped at 2"},
+            "cpu_baseline": cb,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ress(args):
+    from ress_b200 import kernels as K
+    from ress_b200 import layer as LY
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    S = _setup(args.frames, ws, rank, device)
+    L = S["L"]
+    stream = torch.cuda.current_stream(device)
+    out = torch.empty(1, L.H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=device)
+
+    def step():
+        return LY.global_layer(S["q"], S["k"], S["v"], L, S["budget"], S["order"], out=out, shard=S["shard"])
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    K.check_status(device)
+    res = step()
+    torch.cuda.synchronize()
+    sparsity = res.sparsity()
+    attn_flops = _attn_flops(res.lists, res.counts, L)
+
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        ms = _time_region(step, args.steps, stream)
+    torch.cuda.synchronize()
+    barrier()
+    K.check_status(device)
+    t = torch.tensor([ms], device=device)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_step = ms / args.steps
+    value = args.frames * args.steps / (ms / 1000.0)
+
+    # dominant kernel: the sparse attention, timed alone on the same lists
+    qbar, q8, qs = K.pool_quant_q(S["q"], L)
+    _, _, k8, ks, v16, _ = K.pool_quant_kv(S["k"], S["v"], L, pool=False)
+    lists, counts = res.lists, res.counts
+
+    def attn():
+        K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out, out_layout=L)
+
+    for _ in range(3):
+        attn()
+    reps = max(5, min(50, args.steps))
+    attn_ms = _time_region(attn, reps, stream) / reps
+    K.check_status(device)
+    bf16_peak, hbm_peak, peak_src = _peaks()
+    mixed_peak = 2.0 / (1.0 / bf16_peak + 1.0 / (2.0 * bf16_peak))
+    achieved = attn_flops / (attn_ms / 1000.0) / 1e12
+
+    # stage breakdown (one instrumented step)
+    stages = {}
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    ev[0].record(stream)
+    qbar, q8, qs = K.pool_quant_q(S["q"], L)
+    kbar, vbar, k8, ks, v16, km = K.pool_quant_kv(S["k"], S["v"], L)
+    ev[1].record(stream)
+    af, ac = K.predict(qbar, kbar, L.n_cand)
+    base = K.baseline(ac, SPARSE_RATIO).view(1, L.H, L.nq)
+    if S["shard"] is not None:
+        base = S["shard"].gather(base)
+    nts = K.hess_adjust(base, S["budget"].scores_norm, L.n_cand, min_clamp=2)
+    if S["shard"] is not None:
+        nts = nts[:, S["h0"]:S["h0"] + L.H].contiguous()
+    ev[2].record(stream)
+    r = K.restore_swap(af, vbar, S["order"].M, nts.view(-1), L.n_cand, sink_blocks=L.sink_blocks)
+    ev[3].record(stream)
+    K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L)
+    ev[4].record(stream)
+    ev[4].synchronize()
+    for i, name in enumerate(["score_quant", "predict_budget", "restore_swap", "sparse_attn"]):
+        stages[name] = round(ev[i].elapsed_time(ev[i + 1]), 4)
+    hess_ms = None
+    if ws == 1:
+        def step_hess():
+            LY.global_layer(S["q"], S["k"], S["v"], L, S["budget_hess"], S["order_prob"], out=out)
+        step_hess()
+        torch.cuda.synchronize()
+        hess_ms = _time_region(step_hess, max(10, args.steps // 4), stream) / max(10, args.steps // 4)
+
+    # e2e: host buffers in and out through the public layer call
+    qh, kh, vh = (x.cpu().pin_memory() for x in (S["q"], S["k"], S["v"]))
+    oh = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e_step():
+        qd = qh.to(device, non_blocking=True)
+        kd = kh.to(device, non_blocking=True)
+        vd = vh.to(device, non_blocking=True)
+        rr = LY.global_layer(qd, kd, vd, L, S["budget"], S["order"], shard=S["shard"])
+        oh.copy_(rr.out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e_steps = max(3, min(args.steps, 20))
+    e_ms = _time_region(e2e_step, e_steps, stream)
+    te = torch.tensor([e_ms], device=device)
+    if ws > 1:
+        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    e_ms = float(te.item())
+    h2d = sum(x.numel() * x.element_size() for x in (qh, kh, vh))
+    d2h = oh.numel() * oh.element_size()
+    if ws > 1:
+        h2d *= ws
+        d2h *= ws
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = _cpu_baseline(S)
+        except Exception as exc:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"failed: {exc}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_step, "layer_ms": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"cfg2: one VGGT global-attention layer, {args.frames} views x 1374 tokens, "
+                                   f"16 heads x 64, bf16, apply_ress(sparse_ratio={SPARSE_RATIO}, n_iters=5), "
+                                   "HeSS budget lambda=0.5",
+                       "parallelism": f"heads split over {ws} GPU(s)" + (", NCCL all-gather of HeSS baselines" if ws > 1 else ""),
+                       "l2": "inputs larger than L2 (Q/K/V bf16 270 MB)", "sparsity": round(sparsity, 4)},
+            "stages_ms": stages,
+            "apply_hess_layer_ms": hess_ms,
+            "gpu_launches": 10 * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "sparse_attn_kernel", "achieved": achieved,
+                         "peak": mixed_peak, "unit": "TFLOP/s", "frac": achieved / mixed_peak,
+                         "traffic": None, "attn_ms": attn_ms, "attn_tflop_per_launch": attn_flops / 1e12,
+                         "peak_note": f"{peak_src}: harmonic mix of bf16 burst {bf16_peak:.0f} TF/s (PV half) and "
+                                      "int8 = 2x bf16 (QK half)"},
+            "clocks": clk.summary(),
+            "e2e": {"value": args.frames * e_steps / (e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def profile_attn():
+    """Small case for ncu: a 24-frame layer (int8 Q/K + fp16 V = 135 MB,
+    above the 126 MB L2; under 1 GB on the device), two layers."""
+    from ress_b200 import layer as LY
+
+    S = _setup(24, 1, 0, torch.device("cuda", 0))
+    for _ in range(2):
+        LY.global_layer(S["q"], S["k"], S["v"], S["L"], S["budget"], S["order"])
+    torch.cuda.synchronize()
+
+
+def main():
+    args = _args()
+    if args.profile_attn:
+        profile_attn()
+        return
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ress(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -81,7 +81,8 @@ def predict(qbar: torch.Tensor, kbar: torch.Tensor) -> torch.Tensor:
     rows, nq, D = qbar.shape
     nk = kbar.shape[1]
     out = torch.empty(rows, nq, nk, dtype=qbar.dtype)
-    lib().ro_predict(_dt(qbar), _p(qbar.contiguous()), _p(kbar.contiguous()), rows, nq, nk, D, _p(out))
+    qc, kc = qbar.contiguous(), kbar.contiguous()
+    lib().ro_predict(_dt(qc), _p(qc), _p(kc), rows, nq, nk, D, _p(out))
     return out
 
 
@@ -129,7 +130,8 @@ def hess_adjust(counts: torch.Tensor, snorm: torch.Tensor, max_val: int, beta: f
     B, nh, nq = c.shape
     out = torch.empty_like(c)
     omb = float(torch.tensor(1 - beta, dtype=torch.float32))
-    st = lib().ro_hess_adjust(_p(c), _p(snorm.float().contiguous()), B, nh, nq, max_val, _f(omb),
+    sn = snorm.float().contiguous()
+    st = lib().ro_hess_adjust(_p(c), _p(sn), B, nh, nq, max_val, _f(omb),
                               _f(float(beta)), max_iters, min_clamp, _p(out))
     if st != 0:
         raise RuntimeError(f"adjust_attention_selection did not converge in {max_iters} iterations")
@@ -141,7 +143,8 @@ def vbar_metric(vbar_bf16: torch.Tensor, M: torch.Tensor, n_cand: int) -> torch.
     rows, nkp, _ = vb.shape
     nh = M.shape[0]
     tk = torch.empty(rows, n_cand, dtype=torch.int16)
-    lib().ro_vbar_metric(_p(vb), _p(M.float().contiguous()), rows, nh, nkp, n_cand, _p(tk))
+    Mf = M.float().contiguous()
+    lib().ro_vbar_metric(_p(vb), _p(Mf), rows, nh, nkp, n_cand, _p(tk))
     return tk.view(torch.bfloat16)
 
 
@@ -172,8 +175,9 @@ def restore_swap(attn_full: torch.Tensor, vbar_bf16: torch.Tensor, M: torch.Tens
     drop = torch.empty(rows, n_cand, dtype=torch.uint8)
     s = torch.empty(rows, n_cand, dtype=torch.int16)
     nt = nts.to(torch.int32).contiguous().view(-1)
-    lib().ro_restore_swap(_dt(a), _p(a), _p(vb.view(torch.int16)), _p(M.float().contiguous()),
-                          _p(tk.view(torch.int16)), _p(nt), rows, nq, nh, nkp, n_cand, n_iters, _p(fr),
+    vbi, Mf, tki = vb.view(torch.int16), M.float().contiguous(), tk.view(torch.int16)
+    lib().ro_restore_swap(_dt(a), _p(a), _p(vbi), _p(Mf),
+                          _p(tki), _p(nt), rows, nq, nh, nkp, n_cand, n_iters, _p(fr),
                           int(track_best), _p(drop), _p(s))
     return drop.bool(), s.view(torch.bfloat16)
 
@@ -241,9 +245,11 @@ def sparse_attn_rows(q8, qs, k8, ks, v16, lists, counts, samples, sm_scale=None)
     sr = torch.tensor([s[0] for s in samples], dtype=torch.int32)
     sq = torch.tensor([s[1] for s in samples], dtype=torch.int32)
     out = torch.zeros(len(samples), 128, 64, dtype=torch.float32)
-    lib().ro_sparse_attn_rows(_p(q8.contiguous()), _p(k8.contiguous()), _p(v16.float().contiguous()),
-                              _p(qs.contiguous()), _p(ks.contiguous()), Tq, Tk,
-                              _p(lists.to(torch.int32).contiguous()), _p(counts.to(torch.int32).contiguous()),
+    keep = [q8.contiguous(), k8.contiguous(), v16.float().contiguous(), qs.contiguous(), ks.contiguous(),
+            lists.to(torch.int32).contiguous(), counts.to(torch.int32).contiguous()]
+    lib().ro_sparse_attn_rows(_p(keep[0]), _p(keep[1]), _p(keep[2]),
+                              _p(keep[3]), _p(keep[4]), Tq, Tk,
+                              _p(keep[5]), _p(keep[6]),
                               lists.shape[-1], _p(sr), _p(sq), len(samples), _f(sm_scale), _p(out))
     return out
 

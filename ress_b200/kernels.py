@@ -178,8 +178,9 @@ def predict(qbar, kbar, n_cand, full=True, cond=True):
     nkp = kbar.shape[1]
     af = torch.empty(BH, nq, nkp, dtype=qbar.dtype, device=qbar.device) if full else None
     ac = torch.empty(BH, nq, n_cand, dtype=qbar.dtype, device=qbar.device) if cond else None
-    check(_lib.load().ress_predict(_dtype_code(qbar.dtype), _ptr(qbar.contiguous()), _ptr(kbar.contiguous()), BH,
-                                   nq, nkp, n_cand, _ptr(af), _ptr(ac), _stream(qbar.device)), "ress_predict")
+    qc, kc = qbar.contiguous(), kbar.contiguous()
+    check(_lib.load().ress_predict(_dtype_code(qc.dtype), _ptr(qc), _ptr(kc), BH, nq, nkp, n_cand, _ptr(af), _ptr(ac),
+                                   _stream(qbar.device)), "ress_predict")
     return af, ac
 
 
@@ -272,7 +273,8 @@ def restore_swap(attn_full, vbar, M, nts, n_cand, n_iters=5, track_best=True, re
     counts = torch.empty(rows, dtype=torch.int32, device=dev) if want_lists else None
     if ws is None:
         ws = workspace(dev, BH, nkp * KS_K, nkp * KS_K, n_cand)
-    check(_lib.load().ress_restore_swap(_dtype_code(af.dtype), _ptr(af), _ptr(vb), _ptr(M.float().contiguous()),
+    Mf = M.float().contiguous()
+    check(_lib.load().ress_restore_swap(_dtype_code(af.dtype), _ptr(af), _ptr(vb), _ptr(Mf),
                                         _ptr(nt), B, H, nq, nkp, n_cand, n_iters, fr_c, int(track_best), _ptr(drop),
                                         _ptr(s), _ptr(lists), _ptr(counts), width, sink_blocks, lead_blocks,
                                         _ptr(status_word(dev)), _ptr(ws), _stream(dev)), "ress_restore_swap")

@@ -62,6 +62,19 @@ class OrderSpec:
 
 
 @dataclass
+class HeadShard:
+    """This process owns heads [h0, h0 + H_local) of h_total (heads split
+    across GPUs).  HeSS couples the heads of a q-block column, so the
+    baseline counts of all heads are gathered (``gather``: (B, H_local, nq)
+    int32 -> (B, h_total, nq) int32, an NCCL all-gather) and the small
+    re-allocation is computed redundantly on every GPU."""
+
+    h0: int
+    h_total: int
+    gather: object
+
+
+@dataclass
 class LayerResult:
     out: torch.Tensor                  # (B, H, N*P, 64) fp32, full token layout
     layout: K.Layout
@@ -114,7 +127,8 @@ def special_attention(q, k, v, L: K.Layout):
 
 def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSpec, *,
                  num_to_select: torch.Tensor | None = None, budget_fn=None, keep_pooled: bool = False,
-                 lead_blocks: int = 0, out: torch.Tensor | None = None) -> LayerResult:
+                 lead_blocks: int = 0, out: torch.Tensor | None = None,
+                 shard: HeadShard | None = None) -> LayerResult:
     """Run one sparse global-attention layer.  q, k, v: (B, H, N*P, 64) CUDA,
     float32 or bfloat16.  Exactly one of ``budget``, ``num_to_select`` (a
     (B, H, nq) tensor) or ``budget_fn`` (callable(attn_cond) -> (B, H, nq))
@@ -143,7 +157,11 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
         nts = num_to_select.to(device=dev, dtype=torch.int32).reshape(B, H, L.nq).clamp(min=min_sel)
     elif budget is not None:
         base = K.baseline(attn_cond, budget.sparse_ratio, budget.cdf_threshold).view(B, H, L.nq)
-        if budget.kind == "hess":
+        if budget.kind == "hess" and shard is not None:
+            full = shard.gather(base)
+            nts_full = K.hess_adjust(full, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
+            nts = nts_full[:, shard.h0: shard.h0 + H].contiguous()
+        elif budget.kind == "hess":
             nts = K.hess_adjust(base, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
         else:
             nts = base.clamp(min=min_sel)

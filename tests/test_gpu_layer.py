@@ -1,0 +1,116 @@
+"""The fused layer (ress_b200.layer.global_layer) against the oracle chained
+the way ress_attention_forward chains the reference (attention.py:446-659):
+keep lists bit-identical, patch outputs within 2e-2 max / 1e-3 mean abs of
+the fp64 oracle attention, special-token outputs equal to dense attention."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from ress_b200 import kernels as K
+from ress_b200 import layer as LY
+from ress_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    ("cfg1", synth.CONFIG1, torch.float32, "ress", 0.1, None),
+    ("cfg1-hess-cdf", synth.CONFIG1, torch.float32, "prob", 0.5, 0.97),
+    ("6f-bf16-ress", synth.LayerShape(n_frames=6), torch.bfloat16, "ress", 0.5, None),
+    ("cfg2", synth.CONFIG2, torch.bfloat16, "ress", 0.5, None),
+    ("cfg2-hess-cdf", synth.CONFIG2, torch.bfloat16, "prob", 0.5, 0.97),
+]
+_inp = {}
+
+
+def _data(shape, dtype):
+    if (shape, dtype) not in _inp:
+        _inp[(shape, dtype)] = synth.layer_qkv(shape, seed=0, dtype=dtype)
+    return _inp[(shape, dtype)]
+
+
+@pytest.mark.parametrize("name,shape,dtype,mode,sr,cdf", CASES, ids=[c[0] for c in CASES])
+def test_layer_matches_oracle(name, shape, dtype, mode, sr, cdf):
+    q, k, v = _data(shape, dtype)
+    M = synth.metric_from_weight(synth.out_proj_weight())
+    hs = synth.fisher_table(seed=1)[0, 3]
+    L = K.Layout(1, 16, shape.n_frames, shape.n_special, shape.hw)
+    dev = torch.device("cuda", 0)
+    budget = LY.BudgetSpec("hess", sparse_ratio=sr, cdf_threshold=cdf, scores_norm=K.scores_norm(hs))
+    order = LY.OrderSpec("restore_swap", M=M.to(dev)) if mode == "ress" else LY.OrderSpec("probability")
+    res = LY.global_layer(q.to(dev), k.to(dev), v.to(dev), L, budget, order)
+    torch.cuda.synchronize()
+    K.check_status(dev)
+    qp, qsp = synth.split_tokens(q, shape)
+    kp, ks = synth.split_tokens(k, shape)
+    vp, vs = synth.split_tokens(v, shape)
+    o = oracle.layer_select(qp, kp, vp, ks.shape[-2], M, head_scores=hs, mode=mode, sparse_ratio=sr,
+                            cdf_threshold=cdf)
+    assert torch.equal(res.nts.cpu(), o["nts"])
+    assert torch.equal(res.counts.cpu(), o["counts"])
+    lists = res.lists.cpu()
+    for i in range(o["counts"].numel()):
+        c = int(o["counts"][i])
+        assert torch.equal(lists[i, :c], o["lists"][i, :c]), i
+    # attention on sampled rows
+    q8, qs, k8, ksc, _ = oracle.quantize_qk(qp, torch.cat([kp, ks], -2))
+    g = torch.Generator().manual_seed(1)
+    samples = [(int(torch.randint(0, 16, (1,), generator=g)), int(torch.randint(0, L.nq, (1,), generator=g)))
+               for _ in range(12)] + [(15, L.nq - 1)]
+    ref = oracle.sparse_attn_rows(q8, qs, k8, ksc, torch.cat([vp, vs], -2).reshape(16, -1, 64).to(torch.float16),
+                                  o["lists"].view(16, L.nq, -1), o["counts"].view(16, L.nq), samples)
+    out = res.out.cpu()
+    patch, special = synth.split_tokens(out, shape)
+    errs = []
+    for i, (h, qb) in enumerate(samples):
+        n = min(128, L.Tp - qb * 128)
+        errs.append((patch[0, h, qb * 128: qb * 128 + n] - ref[i, :n]).abs().reshape(-1))
+    e = torch.cat(errs)
+    assert e.max().item() < 2e-2, e.max().item()
+    assert e.mean().item() < 1e-3, e.mean().item()
+    # special-token queries: dense attention over all keys (attention.py:404-409)
+    exp = F.scaled_dot_product_attention(qsp.float(), torch.cat([kp, ks], -2).float(),
+                                         torch.cat([vp, vs], -2).float())
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    assert (special - exp).abs().max().item() < tol
+    # sparsity as the reference reports it (sinks counted)
+    width = o["n_cand"] + o["sink_blocks"]
+    assert abs(res.sparsity() - (1 - o["counts"].sum().item() / (o["counts"].numel() * width))) < 1e-12
+
+
+def test_head_split_equals_full():
+    """Heads split into 4 groups with the HeSS baseline exchange emulated on
+    one GPU gives the same lists as the unsplit layer."""
+    shape, dtype = synth.LayerShape(n_frames=6), torch.bfloat16
+    q, k, v = _data(shape, dtype)
+    dev = torch.device("cuda", 0)
+    M = synth.metric_from_weight(synth.out_proj_weight()).to(dev)
+    sn = K.scores_norm(synth.fisher_table(seed=1)[0, 5])
+    budget = LY.BudgetSpec("hess", sparse_ratio=0.5, scores_norm=sn)
+    L = K.Layout(1, 16, shape.n_frames, shape.n_special, shape.hw)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    full = LY.global_layer(qd, kd, vd, L, budget, LY.OrderSpec("restore_swap", M=M))
+    # baselines of every group first (what the all-gather delivers)
+    Lg = K.Layout(1, 4, shape.n_frames, shape.n_special, shape.hw)
+    bases = []
+    for g in range(4):
+        sl = slice(4 * g, 4 * g + 4)
+        qbar, _, _ = K.pool_quant_q(qd[:, sl].contiguous(), Lg, quant=False)
+        kbar, _, _, _, _, _ = K.pool_quant_kv(kd[:, sl].contiguous(), vd[:, sl].contiguous(), Lg, quant=False)
+        _, ac = K.predict(qbar, kbar, Lg.n_cand, full=False)
+        bases.append(K.baseline(ac, 0.5).view(1, 4, -1))
+    gathered = torch.cat(bases, dim=1)
+    for g in range(4):
+        sl = slice(4 * g, 4 * g + 4)
+        shard = LY.HeadShard(h0=4 * g, h_total=16, gather=lambda base, _g=gathered: _g)
+        part = LY.global_layer(qd[:, sl].contiguous(), kd[:, sl].contiguous(), vd[:, sl].contiguous(), Lg, budget,
+                               LY.OrderSpec("restore_swap", M=M[sl]), shard=shard)
+        rows = slice(4 * g * L.nq, (4 * g + 4) * L.nq)
+        assert torch.equal(part.counts, full.counts[rows])
+        w = L.n_cand + L.sink_blocks
+        assert torch.equal(K.lists_to_map(part.lists, part.counts, w), K.lists_to_map(full.lists[rows], full.counts[rows], w))
+        pp, ps = synth.split_tokens(part.out.cpu(), shape)
+        fp, fs = synth.split_tokens(full.out[:, sl].cpu(), shape)
+        assert torch.equal(pp, fp)
+        assert (ps - fs).abs().max().item() < 1e-2
