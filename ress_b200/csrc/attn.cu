@@ -46,7 +46,8 @@ constexpr int OFF_V = OFF_K + NS * K_BYTES;
 constexpr int OFF_P = OFF_V + NS * V_BYTES;
 constexpr int SMEM_TILES = OFF_P + 2 * P_BYTES;
 constexpr int SMEM_BYTES = SMEM_TILES + 1024;  // + alignment slack
-constexpr uint32_t TMEM_COLS = 256;            // S[2] (64 each) + O[2] (64 each)
+constexpr uint32_t TMEM_COLS = 256;            // S[2] (64 each) + O (64), power of two
+constexpr float RESCALE_THRESH = 8.0f;         // lazy rescale when the max grows by > 2^8
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
 
 // ------------------------------------------------------------- PTX wrappers
@@ -138,6 +139,30 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // UMMA shared-memory descriptor (sm100 format: version 1 at bits 46-47,
 // layout type at bits 61-63: 2 = 128B swizzle, 4 = 64B swizzle).
@@ -161,7 +186,7 @@ constexpr uint32_t IDESC_F16 = (1u << 4) | (1u << 16) | ((64u >> 3) << 17) | ((1
 struct Bars {
     uint64_t q_full;
     uint64_t kv_full[NS], kv_empty[NS];
-    uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
+    uint64_t s_full[2], s_free[2], p_full[2], o_full[2];
     uint64_t mma_done;
     uint32_t tmem_base;
     int abort_flag;
@@ -198,7 +223,6 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             mbar_init(&B.s_free[i], 128);
             mbar_init(&B.p_full[i], 128);
             mbar_init(&B.o_full[i], 1);
-            mbar_init(&B.o_free[i], 128);
         }
         mbar_init(&B.mma_done, 1);
         B.abort_flag = 0;
@@ -254,7 +278,6 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             auto issue_pv = [&](int i) -> bool {
                 const int pb = i & 1;
                 if (!wait_bar(&B.p_full[pb], (i >> 1) & 1, abort_flag, status)) return false;
-                if (i >= 2 && !wait_bar(&B.o_free[pb], ((i - 2) >> 1) & 1, abort_flag, status)) return false;
                 fence_after();
                 const uint32_t pa = sP + pb * P_BYTES;
                 const uint32_t va = sV + (i % NS) * V_BYTES;
@@ -262,7 +285,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t ad = make_desc(pa + kk * 32, 16, 1024, LAYOUT_SW128);
                     const uint64_t bd = make_desc(va + kk * 2048, 8192, 1024, LAYOUT_SW128);
-                    mma_f16(tO + pb * 64, ad, bd, IDESC_F16, kk > 0 ? 1u : 0u);
+                    mma_f16(tO, ad, bd, IDESC_F16, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(&B.o_full[pb]);
                 mma_commit(&B.kv_empty[i % NS]);
@@ -292,32 +315,22 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         }
     } else {
         // ------------------------------------------------------------ softmax
-        const int quad = warp & 3;                 // TMEM lane quadrant of this warp
-        const int r = quad * 32 + lane;            // query row within the block
+        // thread = query row = TMEM lane.  S is read once into registers as
+        // float bits of (1.5 * 2^23 + s) (exact for |s| < 2^22; |s| <= 64 *
+        // 127^2), so the scale-and-subtract is one FMA per element.  O
+        // accumulates in TMEM across blocks; it is rescaled only when a row's
+        // maximum grows by more than 2^RESCALE_THRESH (P then stays <= 2^8,
+        // well inside fp16), after waiting for the previous P.V.
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const float qs = qscale[(size_t)bh * nqb + qb];
-        float o[HD];
-#pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = 0.0f;
-        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+        const float MAGIC_F = 12582912.0f;
+        const uint32_t MAGIC_I = 0x4B400000u;
+        float m = -INFINITY, l = 0.0f;
         bool ok = true;
         const uint32_t prow = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
-        auto fold = [&](int i, float alpha) -> bool {
-            const int pb = i & 1;
-            if (!wait_bar_warp(&B.o_full[pb], (i >> 1) & 1, abort_flag, status)) return false;
-            fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t v[16];
-                tmem_ld16(tO + pb * 64 + c * 16 + lane_addr, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int t = 0; t < 16; ++t) o[c * 16 + t] = fmaf(o[c * 16 + t], alpha, __uint_as_float(v[t]));
-            }
-            fence_before();
-            mbar_arrive(&B.o_free[pb]);
-            return true;
-        };
+        const uint32_t rsw = (uint32_t)(r & 7);
         for (int j = 0; j < cnt; ++j) {
             const int sb = j & 1;
             const int kb = lst[j];
@@ -325,62 +338,107 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             const int nvalid = min(64, Tk - kb * 64);
             if (!wait_bar_warp(&B.s_full[sb], (j >> 1) & 1, abort_flag, status)) { ok = false; break; }
             fence_after();
-            int smax = INT_MIN;
+            uint32_t sv[64];
+            tmem_ld32(tS + sb * 64 + lane_addr, sv);
+            tmem_ld32(tS + sb * 64 + 32 + lane_addr, sv + 32);
+            tmem_wait_ld();
+            fence_before();
+            mbar_arrive(&B.s_free[sb]);
+            float fmx;
+            if (nvalid == 64) {
+                float a0 = -INFINITY, a1 = -INFINITY;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t v[16];
-                tmem_ld16(tS + sb * 64 + ch * 16 + lane_addr, v);
-                tmem_wait_ld();
+                for (int t = 0; t < 64; t += 2) {
+                    sv[t] += MAGIC_I;
+                    sv[t + 1] += MAGIC_I;
+                    a0 = fmaxf(a0, __uint_as_float(sv[t]));
+                    a1 = fmaxf(a1, __uint_as_float(sv[t + 1]));
+                }
+                fmx = fmaxf(a0, a1);
+            } else {
+                fmx = -INFINITY;
 #pragma unroll
-                for (int t = 0; t < 16; ++t)
-                    if (ch * 16 + t < nvalid) smax = max(smax, (int)v[t]);
+                for (int t = 0; t < 64; ++t) {
+                    sv[t] += MAGIC_I;
+                    if (t < nvalid) fmx = fmaxf(fmx, __uint_as_float(sv[t]));
+                }
             }
-            const float mx = c * (float)smax;
-            const float m_new = fmaxf(m, mx);
-            const float alpha = exp2f(m - m_new);
+            const float mx = c * (fmx - MAGIC_F);
+            // lazy rescale: keep the old maximum unless it grew by more than the threshold
+            const bool grow = mx > m + RESCALE_THRESH;
+            const float m_new = grow ? mx : m;
+            const float alpha = grow ? ex2(m - m_new) : 1.0f;
+            if (__any_sync(0xffffffffu, grow && j > 0)) {
+                // O holds P.V of blocks < j in units of m: wait for the last of them, rescale in TMEM
+                if (!wait_bar_warp(&B.o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, status)) { ok = false; break; }
+                fence_after();
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                    uint32_t o16[16];
+                    tmem_ld16(tO + ch * 16 + lane_addr, o16);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) o16[t] = __float_as_uint(__uint_as_float(o16[t]) * alpha);
+                    tmem_st16(tO + ch * 16 + lane_addr, o16);
+                }
+                tmem_wait_st();
+            }
+            // P_{j-2} (same shared buffer) must have been consumed by its P.V
+            if (j >= 2 && !wait_bar_warp(&B.o_full[sb], ((j - 2) >> 1) & 1, abort_flag, status)) { ok = false; break; }
+            const float bias = fmaf(-c, MAGIC_F, -m_new);
             float lsum = 0.0f;
             const uint32_t pbase = sP + sb * P_BYTES + prow;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t v[16];
-                tmem_ld16(tS + sb * 64 + ch * 16 + lane_addr, v);
-                tmem_wait_ld();
-                uint32_t h[8];
+            for (int ch = 0; ch < 8; ++ch) {
+                uint32_t h[4];
 #pragma unroll
-                for (int t = 0; t < 16; t += 2) {
-                    float p0 = (ch * 16 + t < nvalid) ? exp2f(fmaf(c, (float)(int)v[t], -m_new)) : 0.0f;
-                    float p1 = (ch * 16 + t + 1 < nvalid) ? exp2f(fmaf(c, (float)(int)v[t + 1], -m_new)) : 0.0f;
+                for (int t = 0; t < 8; t += 2) {
+                    const int i0 = ch * 8 + t;
+                    float p0 = ex2(fmaf(c, __uint_as_float(sv[i0]), bias));
+                    float p1 = ex2(fmaf(c, __uint_as_float(sv[i0 + 1]), bias));
+                    if (nvalid < 64) {
+                        p0 = i0 < nvalid ? p0 : 0.0f;
+                        p1 = i0 + 1 < nvalid ? p1 : 0.0f;
+                    }
+                    lsum += p0 + p1;
                     __half2 hp = __floats2half2_rn(p0, p1);
-                    lsum += __low2float(hp) + __high2float(hp);
                     h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
                 }
-                // two 16-byte chunks (8 keys each) -> swizzled positions
-                const uint32_t c0 = (uint32_t)(2 * ch), c1 = c0 + 1;
-                const uint32_t a0 = pbase + ((c0 ^ (uint32_t)(r & 7)) << 4);
-                const uint32_t a1 = pbase + ((c1 ^ (uint32_t)(r & 7)) << 4);
-                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a0), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
-                             : "memory");
-                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a1), "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7])
+                const uint32_t a = pbase + (((uint32_t)ch ^ rsw) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
                              : "memory");
             }
             fence_before();
-            mbar_arrive(&B.s_free[sb]);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&B.p_full[sb]);
             l = l * alpha + lsum;
             m = m_new;
-            if (j >= 1 && !fold(j - 1, alpha_prev)) { ok = false; break; }
-            alpha_prev = alpha;
         }
-        if (ok && cnt > 0) ok = fold(cnt - 1, alpha_prev);
+        if (ok && cnt > 0) {
+            ok = wait_bar_warp(&B.o_full[(cnt - 1) & 1], ((cnt - 1) >> 1) & 1, abort_flag, status);
+            fence_after();
+        }
         const int t = qb * 128 + r;
-        if (t < Tq) {
-            const long long tt = (long long)(t / out_hw) * (out_hw + out_special) + out_special + (t % out_hw);
-            float *dst = out + (size_t)bh * out_sh + tt * out_st;
-            const float inv = (ok && cnt > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+        const float inv = (ok && cnt > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+        const long long tt = (long long)(t / out_hw) * (out_hw + out_special) + out_special + (t % out_hw);
+        float *dst = out + (size_t)bh * out_sh + tt * out_st;
 #pragma unroll
-            for (int i = 0; i < HD; i += 4)
-                *reinterpret_cast<float4 *>(dst + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+        for (int ch = 0; ch < 4; ++ch) {
+            uint32_t o16[16];
+            if (ok && cnt > 0) {
+                tmem_ld16(tO + ch * 16 + lane_addr, o16);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o16[i] = 0u;
+            }
+            if (t < Tq) {
+#pragma unroll
+                for (int i = 0; i < 16; i += 4)
+                    *reinterpret_cast<float4 *>(dst + ch * 16 + i) =
+                        make_float4(__uint_as_float(o16[i]) * inv, __uint_as_float(o16[i + 1]) * inv,
+                                    __uint_as_float(o16[i + 2]) * inv, __uint_as_float(o16[i + 3]) * inv);
+            }
         }
     }
     fence_before();
