@@ -419,6 +419,384 @@ __global__ void __launch_bounds__(SEL_NT) map_lists_kernel(const uint8_t *__rest
     emit_list<SEL_NT>(keep, width, 0, 0, lists + (size_t)row * list_width, counts + row, list_width, status, red);
 }
 
+// ----------------------------------------------------------------- restore-swap v2
+// The head's vbar stays resident in shared memory (bf16, 16-byte chunks of
+// row k stored at chunk position c ^ (k & 7), so a warp reading one row per
+// thread and 64 threads reading one column are both conflict-free) and one
+// CTA processes up to 8 q-block rows of that head, one 64-thread group (two
+// warps, named barrier 1 + g) per row.  Operation order is that of
+// restore_swap_kernel / the oracle; only the placement of data changes.
+constexpr int G_NT = 64;
+
+__device__ __forceinline__ void gbar(int g) { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(G_NT) : "memory"); }
+
+struct GroupScratch {
+    int hist[256];
+    int red[2];
+    int bin, remaining;
+    float vq[HD], Mvq[HD], g[HD], Mg[HD], Mgb[HD];
+    float tm, sum_pd, G, K, J, bestJ, tqb, tqs;
+    int flag;
+};
+
+__device__ __forceinline__ int gsum(int v, int *red, int g, int t) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    gbar(g);
+    if ((t & 31) == 0) red[t >> 5] = v;
+    gbar(g);
+    return red[0] + red[1];
+}
+
+__device__ __forceinline__ int gscan_excl(int v, int *red, int g, int t, int *total) {
+    const int l = t & 31, w = t >> 5;
+    int x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (l >= o) x += y;
+    }
+    gbar(g);
+    if (l == 31) red[w] = x;
+    gbar(g);
+    *total = red[0] + red[1];
+    return (w == 1 ? red[0] : 0) + x - v;
+}
+
+// block_select_top_m for one 64-thread group (same semantics).
+__device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, int n, int m, uint8_t *sel,
+                                   GroupScratch &sc, int g, int t) {
+    const int chunk = (n + G_NT - 1) / G_NT;
+    const int i0 = t * chunk, i1 = min(n, i0 + chunk);
+    int nv = 0;
+    for (int i = i0; i < i1; ++i) nv += valid[i] ? 1 : 0;
+    const int n_valid = gsum(nv, sc.red, g, t);
+    if (m < 0) m = 0;
+    if (m >= n_valid || m == 0) {
+        const bool all = m > 0;
+        for (int i = i0; i < i1; ++i) sel[i] = (all && valid[i]) ? 1 : 0;
+        gbar(g);
+        return;
+    }
+    uint32_t prefix = 0, pmask = 0;
+    int rem = m;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int b = t; b < 256; b += G_NT) sc.hist[b] = 0;
+        gbar(g);
+        // warp-aggregated histogram: lanes holding the same digit add once
+        for (int j = 0; j < chunk; ++j) {
+            const int i = i0 + j;
+            int bin = -1;
+            if (i < i1) {
+                const uint32_t k = key[i];
+                if (valid[i] && (k & pmask) == prefix) bin = (int)((k >> shift) & 255u);
+            }
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (bin >= 0 && (t & 31) == __ffs(peers) - 1) atomicAdd(&sc.hist[bin], __popc(peers));
+        }
+        gbar(g);
+        if (t < 32) {
+            int c[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { c[j] = sc.hist[255 - 8 * t - j]; sum += c[j]; }
+            int x = sum;
+            for (int o = 1; o < 32; o <<= 1) {
+                int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (t >= o) x += y;
+            }
+            const int before = x - sum;
+            if (before < rem && rem <= x) {
+                int acc = before;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (acc < rem && rem <= acc + c[j]) {
+                        sc.bin = 255 - 8 * t - j;
+                        sc.remaining = rem - acc;
+                    }
+                    acc += c[j];
+                }
+            }
+        }
+        gbar(g);
+        prefix |= ((uint32_t)sc.bin) << shift;
+        pmask |= 255u << shift;
+        rem = sc.remaining;
+        gbar(g);
+    }
+    int eq = 0;
+    for (int i = i0; i < i1; ++i) eq += (valid[i] && key[i] == prefix) ? 1 : 0;
+    int tot;
+    int before = gscan_excl(eq, sc.red, g, t, &tot);
+    for (int i = i0; i < i1; ++i) {
+        uint8_t s = 0;
+        if (valid[i]) {
+            const uint32_t k = key[i];
+            if (k > prefix) s = 1;
+            else if (k == prefix) { s = (before < rem) ? 1 : 0; ++before; }
+        }
+        sel[i] = s;
+    }
+    gbar(g);
+}
+
+__device__ __forceinline__ float vb_at(const uint16_t *vb, int k, int d) {
+    const int c = (d >> 3) ^ (k & 7);
+    return bf16_from_bits(vb[(size_t)k * HD + c * 8 + (d & 7)]);
+}
+__device__ __forceinline__ void vb_row(const uint16_t *vb, int k, float *v) {
+    const uint4 *row = reinterpret_cast<const uint4 *>(vb + (size_t)k * HD);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 u = row[c ^ (k & 7)];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[c * 8 + 2 * i] = __uint_as_float(w[i] << 16);
+            v[c * 8 + 2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+}
+
+// g, Mg, G, K, J of the current drop set, for one group.  The chains run
+// over every candidate with Pd[k] = drop[k] ? P[k] : +0: an accumulator that
+// starts at +0 is left bit-for-bit unchanged by adding a +0 or -0 product in
+// round-to-nearest, so this equals the sparse sum over the dropped entries
+// (the oracle's order) while letting the loads pipeline.
+__device__ void g_drift(GroupScratch &S, const float *P, float *Pd, const uint8_t *drop, const uint16_t *vb,
+                        const float *M, int n_cand, int g, int t) {
+    for (int k = t; k < n_cand; k += G_NT) Pd[k] = drop[k] ? P[k] : 0.0f;
+    gbar(g);
+    float acc = 0.0f, sp = 0.0f;
+    int k = 0;
+    for (; k + 8 <= n_cand; k += 8) {
+        float pv[8], vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) { pv[u] = Pd[k + u]; vv[u] = vb_at(vb, k + u, t); }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc = __fmaf_rn(pv[u], vv[u], acc);
+        if (t == 0) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) sp = __fadd_rn(sp, pv[u]);
+        }
+    }
+    for (; k < n_cand; ++k) {
+        acc = __fmaf_rn(Pd[k], vb_at(vb, k, t), acc);
+        if (t == 0) sp = __fadd_rn(sp, Pd[k]);
+    }
+    if (t == 0) S.sum_pd = bf16r(sp);
+    gbar(g);
+    const float gd = __fsub_rn(__fmul_rn(S.sum_pd, S.vq[t]), bf16r(acc));
+    S.g[t] = gd;
+    gbar(g);
+    float mg = 0.0f;
+#pragma unroll 16
+    for (int j = 0; j < HD; ++j) mg = __fmaf_rn(M[t * HD + j], S.g[j], mg);
+    S.Mg[t] = mg;
+    gbar(g);
+    if (t == 0) {
+        float G = 0.0f;
+        for (int i = 0; i < HD; ++i) G = __fadd_rn(G, __fmul_rn(S.g[i], S.Mg[i]));
+        S.G = G;
+        S.K = clamp_min(__fsub_rn(S.tm, S.sum_pd), 1e-6f);
+        S.J = __fdiv_rn(G, __fmul_rn(S.K, S.K));
+    }
+    gbar(g);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
+    const T *__restrict__ attn, const uint16_t *__restrict__ vb16, const float *__restrict__ tk,
+    const float *__restrict__ Mg_in, const int32_t *__restrict__ nts, int H, int nq, int nkp, int n_cand,
+    int rows_per_cta, int n_iters, Fracs fr, int track_best, uint8_t *__restrict__ drop_out,
+    uint16_t *__restrict__ s_out, int32_t *__restrict__ lists, int32_t *__restrict__ counts, int list_width,
+    int sink_blocks, int lead, int32_t *__restrict__ status, size_t row_bytes) {
+    extern __shared__ __align__(16) unsigned char dyn[];
+    const int ctas_per_head = (nq + rows_per_cta - 1) / rows_per_cta;
+    const int bh = blockIdx.x / ctas_per_head;
+    const int q0 = (blockIdx.x % ctas_per_head) * rows_per_cta;
+    const int h = bh % H;
+    uint16_t *vb = reinterpret_cast<uint16_t *>(dyn);
+    float *M = reinterpret_cast<float *>(dyn + (size_t)nkp * HD * 2);
+    unsigned char *rows_base = reinterpret_cast<unsigned char *>(M + HD * HD);
+    // whole CTA: vbar (swizzled) and M
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(vb16 + (size_t)bh * nkp * HD);
+        uint4 *dst = reinterpret_cast<uint4 *>(vb);
+        for (int i = threadIdx.x; i < nkp * 8; i += blockDim.x) {
+            const int k = i >> 3, c = i & 7;
+            dst[k * 8 + (c ^ (k & 7))] = src[i];
+        }
+        for (int i = threadIdx.x; i < HD * HD; i += blockDim.x) M[i] = Mg_in[(size_t)h * HD * HD + i];
+    }
+    __syncthreads();
+    const int g = threadIdx.x / G_NT, t = threadIdx.x % G_NT;
+    const int q = q0 + g;
+    if (q >= nq) return;
+    const int row = bh * nq + q;
+    unsigned char *rb = rows_base + (size_t)g * row_bytes;
+    GroupScratch &S = *reinterpret_cast<GroupScratch *>(rb);
+    float *P = reinterpret_cast<float *>(rb + ((sizeof(GroupScratch) + 15) & ~(size_t)15));
+    float *Pd = P + nkp;
+    float *ssq = Pd + n_cand;
+    uint32_t *key = reinterpret_cast<uint32_t *>(ssq + n_cand);
+    uint8_t *drop = reinterpret_cast<uint8_t *>(key + n_cand);
+    uint8_t *best = drop + n_cand;
+    uint8_t *valid = best + n_cand;
+    uint8_t *sel = valid + n_cand;
+    uint8_t *sel2 = sel + n_cand;
+
+    for (int k = t; k < nkp; k += G_NT) P[k] = bf16r(DT<T>::load(attn, (size_t)row * nkp + k));
+    gbar(g);
+    {
+        float acc = 0.0f, s = 0.0f;
+        int k = 0;
+        for (; k + 8 <= nkp; k += 8) {
+            float pv[8], vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) { pv[u] = P[k + u]; vv[u] = vb_at(vb, k + u, t); }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = __fmaf_rn(pv[u], vv[u], acc);
+            if (t == 0) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) s = __fadd_rn(s, pv[u]);
+            }
+        }
+        for (; k < nkp; ++k) {
+            acc = __fmaf_rn(P[k], vb_at(vb, k, t), acc);
+            if (t == 0) s = __fadd_rn(s, P[k]);
+        }
+        S.vq[t] = bf16r(acc);
+        if (t == 0) S.tm = bf16r(s);
+    }
+    gbar(g);
+    {
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(bf16r(M[t * HD + j]), S.vq[j], acc);
+        S.Mvq[t] = bf16r(acc);
+    }
+    gbar(g);
+    if (t == 0) {
+        float s = 0.0f;
+        for (int i = 0; i < HD; ++i) s = __fadd_rn(s, bf16r(__fmul_rn(S.Mvq[i], S.vq[i])));
+        S.tqs = bf16r(s);
+    }
+    gbar(g);
+    const float eps4 = bf16r(1e-4f);
+    for (int k = t; k < n_cand; k += G_NT) {
+        float v[HD];
+        vb_row(vb, k, v);
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < HD; ++i) acc = __fmaf_rn(S.Mvq[i], v[i], acc);
+        const float cross = bf16r(acc);
+        float quad = bf16r(__fsub_rn(S.tqs, bf16r(__fmul_rn(2.0f, cross))));
+        quad = bf16r(__fadd_rn(quad, tk[(size_t)bh * n_cand + k]));
+        quad = clamp_min(quad, 0.0f);
+        const float sq = bf16r(__fsqrt_rn(quad));
+        const float sv = bf16r(__fmul_rn(P[k], sq));
+        const float den = clamp_min(bf16r(__fsub_rn(1.0f, P[k])), eps4);
+        ssq[k] = bf16r(__fmul_rn(sv, sv));
+        if (s_out) s_out[(size_t)row * n_cand + k] = bf16bits(sv);
+        key[k] = order_key(bf16r(__fdiv_rn(sv, den)));
+        valid[k] = 1;
+    }
+    gbar(g);
+    const int nt = nts[row];
+    group_select_top_m(key, valid, n_cand, min(nt, n_cand), sel, S, g, t);
+    for (int k = t; k < n_cand; k += G_NT) drop[k] = sel[k] ? 0 : 1;
+    gbar(g);
+    if (track_best) {
+        g_drift(S, P, Pd, drop, vb, M, n_cand, g, t);
+        if (t == 0) S.bestJ = S.J;
+        for (int k = t; k < n_cand; k += G_NT) best[k] = drop[k];
+        gbar(g);
+    }
+    for (int it = 0; it < n_iters; ++it) {
+        const int pic = (int)rintf(__fmul_rn(fr.f[it], (float)nt));
+        g_drift(S, P, Pd, drop, vb, M, n_cand, g, t);
+        if (t == 0) {
+            S.flag = (track_best && S.J < S.bestJ) ? 1 : 0;
+            if (S.flag) S.bestJ = S.J;
+            float tq = 0.0f;
+            for (int d = 0; d < HD; ++d) tq = __fadd_rn(tq, __fmul_rn(S.vq[d], S.Mg[d]));
+            S.tqb = bf16r(tq);
+        }
+        S.Mgb[t] = bf16r(S.Mg[t]);
+        gbar(g);
+        if (S.flag)
+            for (int k = t; k < n_cand; k += G_NT) best[k] = drop[k];
+        const float G = S.G, K = S.K, tqb = S.tqb;
+        int nd = 0, nk = 0, ben = 0;
+        for (int k = t; k < n_cand; k += G_NT) {
+            float v[HD];
+            vb_row(vb, k, v);
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < HD; ++j) acc = __fmaf_rn(v[j], S.Mgb[j], acc);
+            const float tkk = bf16r(acc);
+            const float r = bf16r(__fmul_rn(P[k], bf16r(__fsub_rn(tkk, tqb))));
+            if (drop[k]) {
+                const float rq = knorm_quality(G, K, __fadd_rn(__fmul_rn(2.0f, r), ssq[k]), P[k]);
+                key[k] = order_key(rq);
+                ben |= (rq > 0.0f) ? 1 : 0;
+                ++nd;
+            } else {
+                key[k] = order_key(knorm_quality(G, K, __fsub_rn(ssq[k], __fmul_rn(2.0f, r)), -P[k]));
+                ++nk;
+            }
+            valid[k] = drop[k] ? 0 : 1;
+        }
+        const int n_drop = gsum(nd, S.red, g, t);
+        const int n_kept = gsum(nk, S.red, g, t);
+        const int beneficial = gsum(ben, S.red, g, t) > 0;
+        int cnt = pic;
+        if (beneficial && cnt < 1) cnt = 1;
+        cnt = min(cnt, n_drop);
+        cnt = min(cnt, n_kept);
+        if (!beneficial) cnt = 0;
+        group_select_top_m(key, drop, n_cand, cnt, sel, S, g, t);
+        group_select_top_m(key, valid, n_cand, cnt, sel2, S, g, t);
+        for (int k = t; k < n_cand; k += G_NT) drop[k] = (uint8_t)((drop[k] && !sel[k]) || sel2[k]);
+        gbar(g);
+    }
+    if (track_best) {
+        g_drift(S, P, Pd, drop, vb, M, n_cand, g, t);
+        if (!(S.J < S.bestJ))
+            for (int k = t; k < n_cand; k += G_NT) drop[k] = best[k];
+        gbar(g);
+    }
+    if (drop_out)
+        for (int k = t; k < n_cand; k += G_NT) drop_out[(size_t)row * n_cand + k] = drop[k];
+    if (counts) {
+        // keep list: ascending kept candidates (or leading sinks), then the sink blocks
+        const int chunk = (n_cand + G_NT - 1) / G_NT;
+        const int i0 = t * chunk, i1 = min(n_cand, i0 + chunk);
+        int c = 0;
+        for (int i = i0; i < i1; ++i) c += (!drop[i] || i < lead) ? 1 : 0;
+        int tot;
+        int pos = gscan_excl(c, S.red, g, t, &tot);
+        int32_t *list = lists ? lists + (size_t)row * list_width : nullptr;
+        if (list) {
+            for (int i = i0; i < i1; ++i)
+                if (!drop[i] || i < lead) {
+                    if (pos < list_width) list[pos] = i;
+                    ++pos;
+                }
+            for (int j = t; j < sink_blocks; j += G_NT)
+                if (tot + j < list_width) list[tot + j] = n_cand + j;
+        }
+        if (t == 0) {
+            const int total = tot + sink_blocks;
+            counts[row] = min(total, list_width);
+            if (total > list_width && status) atomicOr(status, RESS_STATUS_LIST_OVERFLOW);
+        }
+    }
+}
+
+static size_t rs2_row_bytes(int nkp, int n_cand) {
+    size_t b = ((sizeof(GroupScratch) + 15) & ~(size_t)15) + (size_t)nkp * 4 + (size_t)n_cand * (4 + 4 + 4 + 5);
+    return (b + 15) & ~(size_t)15;
+}
+
 static size_t rs_smem(int nkp, int n_cand) {
     return (size_t)nkp * 4 + (size_t)n_cand * (4 + 4 + 4 + 5);
 }
@@ -437,6 +815,23 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
                                                                        vb16, tk);
     Fracs fr;
     for (int i = 0; i < MAX_ITERS; ++i) fr.f[i] = i < n_iters ? fracs[i] : 0.0f;
+    {
+        // v2: vbar resident in shared memory, up to 8 rows per CTA
+        const size_t fixed = (size_t)nkp * HD * 2 + (size_t)HD * HD * 4;
+        const size_t rowb = rs2_row_bytes(nkp, n_cand);
+        int R = 8;
+        while (R > 0 && fixed + (size_t)R * rowb > 220 * 1024) --R;
+        if (R >= 2) {
+            const size_t sm2 = fixed + (size_t)R * rowb;
+            auto k2 = restore_swap_v2_kernel<T>;
+            cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2);
+            const int ctas = BH * ((nq + R - 1) / R);
+            k2<<<ctas, R * G_NT, sm2, st>>>((const T *)attn_full, vb16, tk, M, nts, H, nq, nkp, n_cand, R, n_iters, fr,
+                                           track_best, drop, s, lists, counts, list_width, sink_blocks, lead, status,
+                                           rowb);
+            return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+        }
+    }
     size_t sm = rs_smem(nkp, n_cand);
     auto kern = restore_swap_kernel<T>;
     if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
@@ -474,7 +869,8 @@ extern "C" int ress_restore_swap(int dtype, const void *attn_full, const void *v
         return RESS_E_ARG;
     if (counts && (!status || list_width <= 0)) return RESS_E_ARG;
     if (lists && !counts) return RESS_E_ARG;
-    if (rs_smem(nkp, n_cand) > 200 * 1024) return RESS_E_SHAPE;
+    if (rs_smem(nkp, n_cand) > 200 * 1024 && (size_t)nkp * HD * 2 + HD * HD * 4 + 2 * rs2_row_bytes(nkp, n_cand) > 220 * 1024)
+        return RESS_E_SHAPE;
     cudaStream_t st = (cudaStream_t)stream;
     if (dtype == RESS_F32)
         return restore_swap_t<float>(attn_full, vbar, M, nts, B, H, nq, nkp, n_cand, n_iters, fracs,
