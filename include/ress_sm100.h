@@ -44,8 +44,12 @@ enum {
     RESS_E_DTYPE = -2,    /* unsupported dtype */
     RESS_E_SHAPE = -3,    /* shape outside what the kernels support */
     RESS_E_LAUNCH = -4,   /* a kernel launch failed (cudaGetLastError) */
-    RESS_E_NO_DEVICE = -5 /* no sm_100 device / driver entry point missing */
+    RESS_E_NO_DEVICE = -5, /* no sm_100 device / driver entry point missing */
+    RESS_E_SCRATCH = -6    /* ress_restore_swap_noalloc: scratch beyond its static array */
 };
+
+/* size of the static scratch array of ress_restore_swap_noalloc */
+#define RESS_NOALLOC_SCRATCH_BYTES (4u << 20)
 
 /* device status word bits (OR-ed) */
 enum {
@@ -161,6 +165,28 @@ int ress_restore_swap(int dtype, const void *attn_full, const void *vbar, const 
                       const float *fracs, int track_best, uint8_t *drop, uint16_t *s,
                       int32_t *lists, int32_t *counts, int list_width, int sink_blocks,
                       int lead_blocks, int32_t *status, void *workspace, ress_stream_t stream);
+
+/*
+ * ress_restore_swap without the workspace argument, for callers that cannot
+ * allocate device memory (a plain C/FFI host program with no device
+ * allocator, or a process that reserves all device memory at start-up and
+ * must not call cudaMalloc later).  No counterpart in the reference: the
+ * reference always allocates through torch.
+ * Scratch comes from a static __device__ array of RESS_NOALLOC_SCRATCH_BYTES
+ * (4 MiB) held by every GPU that loads the library until exit; problems
+ * needing more (about BH*nkp*128 + BH*n_cand*4 bytes; cfg2 needs 1.4 MiB)
+ * return RESS_E_SCRATCH without launching.  The first call on each device
+ * looks the array's device address up (cudaGetSymbolAddress) with that
+ * device current; make it before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller.
+ * Results are identical to ress_restore_swap's.
+ */
+int ress_restore_swap_noalloc(int dtype, const void *attn_full, const void *vbar, const float *M,
+                              const int32_t *nts, int B, int H, int nq, int nkp, int n_cand,
+                              int n_iters, const float *fracs, int track_best, uint8_t *drop,
+                              uint16_t *s, int32_t *lists, int32_t *counts, int list_width,
+                              int sink_blocks, int lead_blocks, int32_t *status,
+                              ress_stream_t stream);
 
 /*
  * a.11 for the probability order (apply_sparse_vggt / apply_hess): keep the

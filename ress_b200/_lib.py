@@ -14,6 +14,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libress_sm100.so")
 
 RESS_OK = 0
+RESS_E_SCRATCH = -6
+NOALLOC_SCRATCH_BYTES = 4 << 20
 RESS_F32, RESS_BF16 = 0, 1
 STATUS_HESS_NO_CONVERGENCE = 1
 STATUS_ATTN_WAIT_TIMEOUT = 2
@@ -38,6 +40,8 @@ SIGNATURES = {
     "ress_hess_adjust": (_I, [_P, _P, _I, _I, _I, _I, _F, _F, _I, _I, _P, _P, _P]),
     "ress_restore_swap": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P,
                                _P, _P, _I, _I, _I, _P, _P, _P]),
+    "ress_restore_swap_noalloc": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P,
+                                       _P, _P, _I, _I, _I, _P, _P]),
     "ress_select_prob": (_I, [_I, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _P, _P]),
     "ress_top_m_mask": (_I, [_I, _P, _P, _I, _I, _I, _P, _P]),
     "ress_round_step": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F,

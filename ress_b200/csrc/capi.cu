@@ -12,6 +12,7 @@ extern "C" const char *ress_error_string(int code) {
         case RESS_E_SHAPE: return "shape outside the supported range";
         case RESS_E_LAUNCH: return "kernel launch failed";
         case RESS_E_NO_DEVICE: return "CUDA driver entry point unavailable";
+        case RESS_E_SCRATCH: return "problem needs more scratch than the 4 MiB static array of ress_restore_swap_noalloc";
         default: return "unknown error";
     }
 }

@@ -1,0 +1,68 @@
+// noalloc.cu -- ress_restore_swap_noalloc: the restore-swap entry point for
+// callers that cannot allocate device memory.
+//
+// ress_restore_swap needs a scratch buffer (a bf16 copy of the pooled values
+// and one fp32 term per candidate block) that its caller normally allocates.
+// Some callers have no way to do that: a host program that reaches this
+// library through a plain C/FFI binding and owns no device allocator, or a
+// serving process that reserves all of its device memory up front and treats
+// any later cudaMalloc (which can fail, and which synchronises the device) as
+// an error.  For them this entry point uses a fixed scratch array that lives
+// in the library itself.
+//
+// The array is a file-scope __device__ variable of RESS_NOALLOC_SCRATCH_BYTES
+// (4 MiB).  Every GPU on which the library is loaded holds its own copy until
+// the process exits.  Host code cannot use the array's name as a device
+// address, so the first call made on each device looks the address up with
+// cudaGetSymbolAddress while that device is current and caches it; make that
+// first call before any stream capture begins.  Problems whose scratch would
+// exceed the array are rejected with RESS_E_SCRATCH before anything is
+// launched.  All calls share the one array and it keeps whatever the last
+// call wrote: nothing in it has to start at zero (each call writes every
+// byte it later reads), but calls whose kernels overlap on the GPU -- from
+// different streams or host threads at the same time -- race on it and must
+// be serialised by the caller.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_restore_swap_scratch[RESS_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+void *g_scratch_addr[kMaxDevices] = {nullptr};
+
+// Same layout ress_restore_swap uses inside its workspace: the bf16 copy of
+// vbar at offset 0, then (256-byte aligned) one fp32 term per candidate.
+size_t restore_swap_scratch_bytes(int BH, int nkp, int n_cand) {
+    const size_t vb = ((size_t)BH * nkp * 64 * 2 + 255) & ~(size_t)255;
+    return vb + (size_t)BH * n_cand * sizeof(float);
+}
+
+}  // namespace
+
+extern "C" int ress_restore_swap_noalloc(int dtype, const void *attn_full, const void *vbar, const float *M,
+                                         const int32_t *nts, int B, int H, int nq, int nkp, int n_cand,
+                                         int n_iters, const float *fracs, int track_best, uint8_t *drop,
+                                         uint16_t *s, int32_t *lists, int32_t *counts, int list_width,
+                                         int sink_blocks, int lead_blocks, int32_t *status, ress_stream_t stream) {
+    if (B <= 0 || H <= 0 || nkp <= 0 || n_cand <= 0) return RESS_E_ARG;
+    if (restore_swap_scratch_bytes(B * H, nkp, n_cand) > (size_t)RESS_NOALLOC_SCRATCH_BYTES) return RESS_E_SCRATCH;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return RESS_E_NO_DEVICE;
+    void *scratch;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if (g_scratch_addr[dev] == nullptr) {
+            void *addr = nullptr;
+            if (cudaGetSymbolAddress(&addr, g_restore_swap_scratch) != cudaSuccess || addr == nullptr)
+                return RESS_E_NO_DEVICE;
+            g_scratch_addr[dev] = addr;
+        }
+        scratch = g_scratch_addr[dev];
+    }
+    return ress_restore_swap(dtype, attn_full, vbar, M, nts, B, H, nq, nkp, n_cand, n_iters, fracs, track_best, drop,
+                             s, lists, counts, list_width, sink_blocks, lead_blocks, status, scratch, stream);
+}
