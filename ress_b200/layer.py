@@ -128,7 +128,7 @@ def special_attention(q, k, v, L: K.Layout):
 def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSpec, *,
                  num_to_select: torch.Tensor | None = None, budget_fn=None, keep_pooled: bool = False,
                  lead_blocks: int = 0, out: torch.Tensor | None = None,
-                 shard: HeadShard | None = None) -> LayerResult:
+                 shard: HeadShard | None = None, joint_select_fn=None, map_hook=None) -> LayerResult:
     """Run one sparse global-attention layer.  q, k, v: (B, H, N*P, 64) CUDA,
     float32 or bfloat16.  Exactly one of ``budget``, ``num_to_select`` (a
     (B, H, nq) tensor) or ``budget_fn`` (callable(attn_cond) -> (B, H, nq))
@@ -153,6 +153,24 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
     need_full = order.kind == "restore_swap" or keep_pooled
     attn_full, attn_cond = K.predict(qbar, kbar, n_cand, full=need_full, cond=True)
     min_sel = min(MIN_NUM_TO_SELECT, n_cand)
+    width = n_cand + L.sink_blocks
+    if joint_select_fn is not None:
+        # one-shot joint selection (attention.py:501-508): the callable returns the final map
+        fm = joint_select_fn(attn_cond.view(B, H, L.nq, n_cand), vbar.view(B, H, L.nkp, 64)[:, :, :n_cand],
+                             L.sink_blocks)
+        if map_hook is not None:
+            fm = map_hook(fm.view(B, H, L.nq, width), attn_cond.view(B, H, L.nq, n_cand))
+        lists, counts = K.map_to_lists(fm.reshape(-1, width))
+        if out is None:
+            out = torch.empty(B, H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=dev)
+        K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out, out_layout=L)
+        main.wait_stream(side)
+        if x_special is not None:
+            x_special.record_stream(main)
+            view = out.view(B, H, L.frames, L.special + L.hw, 64)
+            view[:, :, :, : L.special] = x_special.view(B, H, L.frames, L.special, 64).float()
+        return LayerResult(out=out, layout=L, lists=lists, counts=counts, nts=None, attn_full=attn_full,
+                           attn_cond=attn_cond, vbar=vbar)
     if num_to_select is not None:
         nts = num_to_select.to(device=dev, dtype=torch.int32).reshape(B, H, L.nq).clamp(min=min_sel)
     elif budget is not None:
@@ -188,6 +206,11 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
     else:
         raise ValueError(order.kind)
 
+    if map_hook is not None:
+        fm = K.lists_to_map(r["lists"], r["counts"], width).view(B, H, L.nq, width)
+        fm = map_hook(fm, attn_cond.view(B, H, L.nq, n_cand))
+        lists, counts = K.map_to_lists(fm.reshape(-1, width))
+        r = dict(lists=lists, counts=counts)
     if out is None:
         out = torch.empty(B, H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=dev)
     K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L)
