@@ -47,6 +47,7 @@ def _args():
     ap.add_argument("--frames", type=int, default=N_FRAMES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-attn", action="store_true", help="one small layer, for ncu")
+    ap.add_argument("--eager", action="store_true", help="time eager calls instead of CUDA-graph replays")
     return ap.parse_args()
 
 
@@ -142,15 +143,9 @@ def _setup(frames, world, rank, device):
     sn = K.scores_norm(head_scores).to(device)
     shard = None
     if world > 1:
-        import torch.distributed as dist
+        from ress_b200 import shard as SH
 
-        def gather(base):
-            out = torch.empty(world * base.numel(), dtype=base.dtype, device=base.device)
-            dist.all_gather_into_tensor(out, base.contiguous().view(-1))
-            B, Hl, nq = base.shape
-            return out.view(world, B, Hl, nq).permute(1, 0, 2, 3).reshape(B, world * Hl, nq).contiguous()
-
-        shard = LY.HeadShard(h0=h0, h_total=H, gather=gather)
+        shard = SH.make_head_shard(H, world, rank)
     budget = LY.BudgetSpec("hess", sparse_ratio=SPARSE_RATIO, cdf_threshold=None, scores_norm=sn)
     budget_hess = LY.BudgetSpec("hess", sparse_ratio=SPARSE_RATIO, cdf_threshold=CDF, scores_norm=sn)
     order = LY.OrderSpec("restore_swap", M=M, n_iters=5, track_best=True)
@@ -263,20 +258,31 @@ def run_ress(args):
     stream = torch.cuda.current_stream(device)
     out = torch.empty(1, L.H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=device)
 
-    def step():
+    def eager_step():
         return LY.global_layer(S["q"], S["k"], S["v"], L, S["budget"], S["order"], out=out, shard=S["shard"])
 
     def barrier():
         if ws > 1:
             torch.distributed.barrier()
 
+    res = eager_step()
+    torch.cuda.synchronize()
+    K.check_status(device)
+    graph = None
+    if args.eager:
+        step = eager_step
+    else:
+        graph = LY.CapturedLayer(eager_step)
+        step = graph.replay
+        res = graph.result
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
     K.check_status(device)
-    res = step()
-    torch.cuda.synchronize()
-    sparsity = res.sparsity()
+    kept = res.counts.sum().to(torch.float64)
+    if ws > 1:
+        torch.distributed.all_reduce(kept)
+    sparsity = 1.0 - float(kept.item()) / float(res.counts.numel() * ws * res.width)
     attn_flops = _attn_flops(res.lists, res.counts, L)
 
     barrier()
@@ -383,6 +389,7 @@ def run_ress(args):
                                    f"16 heads x 64, bf16, apply_ress(sparse_ratio={SPARSE_RATIO}, n_iters=5), "
                                    "HeSS budget lambda=0.5",
                        "parallelism": f"heads split over {ws} GPU(s)" + (", NCCL all-gather of HeSS baselines" if ws > 1 else ""),
+                       "launch": "eager calls" if args.eager else "one CUDA graph replay per step (layer captured once)",
                        "l2": "inputs larger than L2 (Q/K/V bf16 270 MB)", "sparsity": round(sparsity, 4)},
             "stages_ms": stages,
             "apply_hess_layer_ms": hess_ms,
@@ -398,6 +405,8 @@ def run_ress(args):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    del graph, step
+    torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -495,13 +495,7 @@ extern "C" int ress_sparse_attn(const int8_t *q8, const float *qscale, const int
         !attn::make_map(&tv, v16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Tk, BH, 64, CU_TENSOR_MAP_SWIZZLE_128B))
         return RESS_E_NO_DEVICE;
     const int nqb = (Tq + 127) / 128, nkb = (Tk + 63) / 64;
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(attn::sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 attn::SMEM_BYTES) != cudaSuccess)
-            return RESS_E_LAUNCH;
-        attr_set = true;
-    }
+    set_smem_attr((const void *)attn::sparse_attn_kernel, attn::SMEM_BYTES);
     const float log2e = 1.4426950408889634f;
     attn::sparse_attn_kernel<<<BH * nqb, attn::NT, attn::SMEM_BYTES, (cudaStream_t)stream>>>(
         tq, tk, tv, qscale, kscale, nqb, nkb, Tq, Tk, lists, counts, list_width, sm_scale * log2e, out, out_sh,

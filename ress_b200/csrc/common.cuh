@@ -19,6 +19,24 @@ constexpr int HD = 64;      // head dimension (fixed by the kernels)
 constexpr int KS_Q = 128;   // query block (reference attention.py:37)
 constexpr int KS_K = 64;    // key block (attention.py:38-39)
 
+// Raise a kernel's dynamic shared-memory limit once per (device, kernel,
+// size): the attribute sticks to the function in a device's context, so
+// later launches skip the driver call.
+inline void set_smem_attr(const void *kern, size_t bytes) {
+    if (bytes <= 48 * 1024) return;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static thread_local const void *last_k[64] = {nullptr};
+    static thread_local int last_d[64] = {0};
+    static thread_local size_t last_b[64] = {0};
+    const unsigned slot = (unsigned)((((uintptr_t)kern >> 4) + (uintptr_t)dev * 17u) & 63u);
+    if (last_k[slot] == kern && last_d[slot] == dev && last_b[slot] >= bytes) return;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    last_k[slot] = kern;
+    last_d[slot] = dev;
+    last_b[slot] = bytes;
+}
+
 // ---------------------------------------------------------------- rounding
 __device__ __forceinline__ float bf16r(float x) {
     return __bfloat162float(__float2bfloat16_rn(x));

@@ -399,7 +399,7 @@ static int predict_t(const void *qbar, const void *kbar, int BH, int nq, int nkp
     if (smem(rows) > 220 * 1024) return RESS_E_SHAPE;
     size_t sm = smem(rows);
     auto kern = predict_kernel<T>;
-    if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    set_smem_attr((const void *)kern, sm);
     dim3 grid((nq + rows - 1) / rows, BH);
     kern<<<grid, PRED_NT, sm, s>>>((const T *)qbar, (const T *)kbar, nq, nkp, n_cand, rows, 0.125f, (T *)attn_full,
                                    (T *)attn_cond);
@@ -414,7 +414,7 @@ static int baseline_t(const void *cond, int rows, int n, int use_cdf, float cdf_
     if (!use_cdf) sort_n = 0;
     size_t sm = (size_t)sort_n * sizeof(float);
     auto kern = baseline_kernel<T>;
-    if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    set_smem_attr((const void *)kern, sm);
     kern<<<rows, PRED_NT, sm, s>>>((const T *)cond, n, use_cdf, cdf_value, topk, sort_n, out);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }

@@ -824,7 +824,7 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
         if (R >= 2) {
             const size_t sm2 = fixed + (size_t)R * rowb;
             auto k2 = restore_swap_v2_kernel<T>;
-            cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2);
+            set_smem_attr((const void *)k2, sm2);
             const int ctas = BH * ((nq + R - 1) / R);
             k2<<<ctas, R * G_NT, sm2, st>>>((const T *)attn_full, vb16, tk, M, nts, H, nq, nkp, n_cand, R, n_iters, fr,
                                            track_best, drop, s, lists, counts, list_width, sink_blocks, lead, status,
@@ -834,7 +834,7 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
     }
     size_t sm = rs_smem(nkp, n_cand);
     auto kern = restore_swap_kernel<T>;
-    if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    set_smem_attr((const void *)kern, sm);
     kern<<<rows, SEL_NT, sm, st>>>((const T *)attn_full, vb16, tk, M, nts, H, nq, nkp, n_cand, n_iters,
                                    fr, track_best, drop, s, lists, counts, list_width, sink_blocks, lead,
                                    status);
@@ -847,7 +847,7 @@ static int topm_t(const void *q, const int32_t *cnts, int rows, int n, int large
                   int32_t *status, cudaStream_t st) {
     size_t sm = (size_t)n * 6;
     auto kern = topm_kernel<T>;
-    if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    set_smem_attr((const void *)kern, sm);
     kern<<<rows, SEL_NT, sm, st>>>((const T *)q, cnts, n, largest, sink_blocks, lead, out, lists, counts,
                                    list_width, status);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
@@ -932,7 +932,7 @@ extern "C" int ress_round_step(const void *p, const void *term_k, const void *s_
 #define RESS_ROUND(TP, TS)                                                                              \
     do {                                                                                                \
         auto kern = round_kernel<TP, TS>;                                                               \
-        if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm); \
+        set_smem_attr((const void *)kern, sm); \
         kern<<<rows, SEL_NT, sm, st>>>((const TP *)p, (const TP *)term_k, (const TS *)s_sq, term_q, drop,  \
                                        per_iter, gn, km, n, raw_bf16, q_bf16, knorm, k_eps, new_drop,    \
                                        restore_count);                                                  \
@@ -953,7 +953,7 @@ extern "C" int ress_map_to_lists(const uint8_t *map, int rows, int width, int32_
     if (rows == 0) return RESS_OK;
     if (width > 200 * 1024) return RESS_E_SHAPE;
     size_t sm = (size_t)width;
-    if (sm > 48 * 1024) cudaFuncSetAttribute(map_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    set_smem_attr((const void *)map_lists_kernel, sm);
     map_lists_kernel<<<rows, SEL_NT, sm, (cudaStream_t)stream>>>(map, width, lists, counts, list_width, status);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }

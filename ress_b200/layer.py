@@ -45,7 +45,7 @@ class BudgetSpec:
     sparse_ratio: float | None = None
     cdf_threshold: float | None = None
     beta: float = 1.0
-    scores_norm: torch.Tensor | None = None  # (H,) for "hess"
+    scores_norm: torch.Tensor | None = None  # (H,) fp32 for "hess"; on the layer's device for graph capture
 
 
 @dataclass
@@ -103,6 +103,15 @@ class LayerResult:
 
 
 _random_gens = {}
+_side_streams = {}
+
+
+def _side_stream(dev):
+    st = _side_streams.get(dev)
+    if st is None:
+        st = torch.cuda.Stream(device=dev)
+        _side_streams[dev] = st
+    return st
 
 
 def _random_gen(device):
@@ -141,12 +150,14 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
     n_cand = L.n_cand
     ws = K.workspace(dev, B * H, L.Tp, L.Tk, n_cand)
     main = torch.cuda.current_stream(dev)
-    side = torch.cuda.Stream(device=dev)
+    capturing = torch.cuda.is_current_stream_capturing()
+    side = _side_stream(dev)
     side.wait_stream(main)
     with torch.cuda.stream(side):
         x_special = special_attention(q, k, v, L)
-    for t in (q, k, v):
-        t.record_stream(side)
+    if not capturing:
+        for t in (q, k, v):
+            t.record_stream(side)
 
     qbar, q8, qs = K.pool_quant_q(q, L)
     kbar, vbar, k8, ks, v16, km = K.pool_quant_kv(k, v, L, ws=ws)
@@ -166,7 +177,8 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
         K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out, out_layout=L)
         main.wait_stream(side)
         if x_special is not None:
-            x_special.record_stream(main)
+            if not capturing:
+                x_special.record_stream(main)
             view = out.view(B, H, L.frames, L.special + L.hw, 64)
             view[:, :, :, : L.special] = x_special.view(B, H, L.frames, L.special, 64).float()
         return LayerResult(out=out, layout=L, lists=lists, counts=counts, nts=None, attn_full=attn_full,
@@ -216,11 +228,39 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
     K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L)
     main.wait_stream(side)
     if x_special is not None:
-        x_special.record_stream(main)
+        if not capturing:
+            x_special.record_stream(main)
         view = out.view(B, H, L.frames, L.special + L.hw, 64)
         view[:, :, :, : L.special] = x_special.view(B, H, L.frames, L.special, 64).float()
     return LayerResult(out=out, layout=L, lists=r["lists"], counts=r["counts"], nts=nts,
                        attn_full=attn_full, attn_cond=attn_cond, vbar=vbar)
+
+
+class CapturedLayer:
+    """A layer call captured once into a CUDA graph and replayed.
+
+    ``fn`` must read its inputs from and write its output to tensors that stay
+    alive (static buffers); every kernel of the layer is stream-ordered with
+    no host synchronisation, so the whole step -- the library's kernels, the
+    side-stream SDPA and, under a head split, the NCCL all-gather -- becomes
+    one graph launch.  Replays give the same bits as eager calls."""
+
+    def __init__(self, fn, warmup: int = 2):
+        dev = torch.cuda.current_device()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.result = fn()
+
+    def replay(self):
+        self.graph.replay()
+        return self.result
 
 
 def dense_layer(q, k, v, L: K.Layout) -> torch.Tensor:

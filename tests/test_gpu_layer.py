@@ -114,3 +114,24 @@ def test_head_split_equals_full():
         fp, fs = synth.split_tokens(full.out[:, sl].cpu(), shape)
         assert torch.equal(pp, fp)
         assert (ps - fs).abs().max().item() < 1e-2
+
+
+def test_cuda_graph_replay_equals_eager():
+    """The layer captured in a CUDA graph (library kernels, side-stream SDPA)
+    replays to the same bits as the eager call."""
+    shape, dtype = synth.LayerShape(n_frames=6), torch.bfloat16
+    q, k, v = (t.cuda() for t in _data(shape, dtype))
+    dev = q.device
+    M = synth.metric_from_weight(synth.out_proj_weight()).to(dev)
+    sn = K.scores_norm(synth.fisher_table(seed=1)[0, 1]).to(dev)
+    budget = LY.BudgetSpec("hess", sparse_ratio=0.5, scores_norm=sn)
+    L = K.Layout(1, 16, shape.n_frames, shape.n_special, shape.hw)
+    order = LY.OrderSpec("restore_swap", M=M)
+    eager = LY.global_layer(q, k, v, L, budget, order)
+    out = torch.empty_like(eager.out)
+    cap = LY.CapturedLayer(lambda: LY.global_layer(q, k, v, L, budget, order, out=out))
+    for _ in range(2):
+        r = cap.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(r.out, eager.out)
+        assert torch.equal(r.counts, eager.counts)
