@@ -18,9 +18,11 @@
 //               PV_j = P_j V_j with kind::f16 (fp16 x fp16 -> fp32) into a
 //               second TMEM double buffer.
 //   warps 2-5   softmax: thread = query row = TMEM lane.  Reads S_j with
-//               tcgen05.ld, keeps the running max / sum, writes P_j (fp16)
-//               into shared memory in the 128B-swizzled K-major layout the
-//               MMA reads, and folds PV_{j-1} into fp32 registers.
+//               tcgen05.ld, keeps the running max, writes P_j (fp16) into
+//               shared memory in the 128B-swizzled K-major layout the MMA
+//               reads.  O accumulates in TMEM; the P.V MMA has N = 80, the
+//               extra 16 B columns being ones, so O's columns 64..79 carry
+//               the softmax denominator sum(P) at no CUDA-core cost.
 // Every mbarrier wait is bounded (~2 s); on expiry the CTA raises an abort
 // flag, records RESS_STATUS_ATTN_WAIT_TIMEOUT, drains its own in-flight
 // copies and MMAs, frees its tensor memory and exits.
@@ -44,9 +46,12 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + Q_BYTES;
 constexpr int OFF_V = OFF_K + NS * K_BYTES;
 constexpr int OFF_P = OFF_V + NS * V_BYTES;
-constexpr int SMEM_TILES = OFF_P + 2 * P_BYTES;
+constexpr int ONES_BYTES = 64 * 64 * 2;  // fp16 ones: the 80-column P.V's row-sum columns
+constexpr int OFF_ONES = OFF_P + 2 * P_BYTES;
+constexpr int SMEM_TILES = OFF_ONES + ONES_BYTES;
 constexpr int SMEM_BYTES = SMEM_TILES + 1024;  // + alignment slack
-constexpr uint32_t TMEM_COLS = 256;            // S[2] (64 each) + O (64), power of two
+constexpr uint32_t TMEM_COLS = 256;            // S[2] (64 each) + O (80), power of two
+constexpr int O_COLS = 80;                      // 64 output columns + 16 columns of sum(P)
 constexpr float RESCALE_THRESH = 8.0f;         // lazy rescale when the max grows by > 2^8
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
 
@@ -80,6 +85,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait with a suspend-time hint: a waiting thread is parked by the
+// hardware until the phase completes or the hint (ns) elapses, instead of
+// spinning through issue slots the softmax warps need.
+constexpr uint32_t SUSPEND_NS = 200000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity), "r"(SUSPEND_NS)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait: false when the CTA aborted or this wait expired.
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
                                          int32_t *status) {
@@ -87,7 +107,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
-        if (mbar_try_wait(addr, parity)) return true;
+        if (mbar_try_wait_sleep(addr, parity)) return true;
         if (*abort_flag) return false;
         if (globaltimer() - t0 > TIMEOUT_NS) {
             *abort_flag = 1;
@@ -158,6 +178,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -181,7 +206,8 @@ constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
 //   kind::i8 : D s32 (bits 4-5 = 2), A/B signed (bits 7, 10), both K-major.
 //   kind::f16: D f32 (1), A/B f16 (0), A K-major, B MN-major (bit 16).
 constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
-constexpr uint32_t IDESC_F16 = (1u << 4) | (1u << 16) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+//   P.V uses N = 80: the 16 extra B columns are ones, so O columns 64..79 hold sum(P).
+constexpr uint32_t IDESC_F16 = (1u << 4) | (1u << 16) | ((80u >> 3) << 17) | ((128u >> 4) << 24);
 
 struct Bars {
     uint64_t q_full;
@@ -205,6 +231,13 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     const uint32_t sK = smem_u32(smem + OFF_K);
     const uint32_t sV = smem_u32(smem + OFF_V);
     const uint32_t sP = smem_u32(smem + OFF_P);
+    const uint32_t sOnes = smem_u32(smem + OFF_ONES);
+    {
+        // ones tile (fp16 1.0), read by the tensor core through the async proxy
+        uint4 *o4 = reinterpret_cast<uint4 *>(smem + OFF_ONES);
+        for (int i = threadIdx.x; i < ONES_BYTES / 16; i += NT) o4[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x;
     const int bh = row / nqb, qb = row - bh * nqb;
@@ -284,7 +317,8 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t ad = make_desc(pa + kk * 32, 16, 1024, LAYOUT_SW128);
-                    const uint64_t bd = make_desc(va + kk * 2048, 8192, 1024, LAYOUT_SW128);
+                    // B = [V tile | ones tile]: the second 128B-wide atom along N sits LBO bytes on
+                    const uint64_t bd = make_desc(va + kk * 2048, sOnes - va, 1024, LAYOUT_SW128);
                     mma_f16(tO, ad, bd, IDESC_F16, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(&B.o_full[pb]);
@@ -327,7 +361,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         const float qs = qscale[(size_t)bh * nqb + qb];
         const float MAGIC_F = 12582912.0f;
         const uint32_t MAGIC_I = 0x4B400000u;
-        float m = -INFINITY, l = 0.0f;
+        float m = -INFINITY;
         bool ok = true;
         const uint32_t prow = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
         const uint32_t rsw = (uint32_t)(r & 7);
@@ -348,11 +382,13 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             if (nvalid == 64) {
                 float a0 = -INFINITY, a1 = -INFINITY;
 #pragma unroll
-                for (int t = 0; t < 64; t += 2) {
+                for (int t = 0; t < 64; t += 4) {
                     sv[t] += MAGIC_I;
                     sv[t + 1] += MAGIC_I;
-                    a0 = fmaxf(a0, __uint_as_float(sv[t]));
-                    a1 = fmaxf(a1, __uint_as_float(sv[t + 1]));
+                    sv[t + 2] += MAGIC_I;
+                    sv[t + 3] += MAGIC_I;
+                    a0 = max3(a0, __uint_as_float(sv[t]), __uint_as_float(sv[t + 1]));
+                    a1 = max3(a1, __uint_as_float(sv[t + 2]), __uint_as_float(sv[t + 3]));
                 }
                 fmx = fmaxf(a0, a1);
             } else {
@@ -373,7 +409,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                 if (!wait_bar_warp(&B.o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, status)) { ok = false; break; }
                 fence_after();
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
+                for (int ch = 0; ch < O_COLS / 16; ++ch) {
                     uint32_t o16[16];
                     tmem_ld16(tO + ch * 16 + lane_addr, o16);
                     tmem_wait_ld();
@@ -386,7 +422,6 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             // P_{j-2} (same shared buffer) must have been consumed by its P.V
             if (j >= 2 && !wait_bar_warp(&B.o_full[sb], ((j - 2) >> 1) & 1, abort_flag, status)) { ok = false; break; }
             const float bias = fmaf(-c, MAGIC_F, -m_new);
-            float lsum = 0.0f;
             const uint32_t pbase = sP + sb * P_BYTES + prow;
 #pragma unroll
             for (int ch = 0; ch < 8; ++ch) {
@@ -400,7 +435,6 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                         p0 = i0 < nvalid ? p0 : 0.0f;
                         p1 = i0 + 1 < nvalid ? p1 : 0.0f;
                     }
-                    lsum += p0 + p1;
                     __half2 hp = __floats2half2_rn(p0, p1);
                     h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
                 }
@@ -411,7 +445,6 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             fence_before();
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&B.p_full[sb]);
-            l = l * alpha + lsum;
             m = m_new;
         }
         if (ok && cnt > 0) {
@@ -419,6 +452,13 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             fence_after();
         }
         const int t = qb * 128 + r;
+        float l = 0.0f;  // sum(P) from the ones columns of O
+        if (ok && cnt > 0) {
+            uint32_t o16[16];
+            tmem_ld16(tO + 64 + lane_addr, o16);
+            tmem_wait_ld();
+            l = __uint_as_float(o16[0]);
+        }
         const float inv = (ok && cnt > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
         const long long tt = (long long)(t / out_hw) * (out_hw + out_special) + out_special + (t % out_hw);
         float *dst = out + (size_t)bh * out_sh + tt * out_st;
