@@ -9,20 +9,27 @@
 // non-causal, keys past Tk masked.  Q and K arrive as per-block int8 with
 // fp32 scales (ress_score_quant), V as fp16.
 //
-// One CTA per row, 6 warps:
+// One CTA per row, 7 warps:
 //   warp 0      TMA producer: Q tile once, then K/V tiles of the listed
 //               blocks through an NS-stage ring (cp.async.bulk.tensor);
 //               also allocates / frees the CTA's tensor memory.
-//   warp 1      MMA issuer (one thread): S_j = Q K_j^T with
-//               tcgen05.mma kind::i8 into a TMEM double buffer, and
-//               PV_j = P_j V_j with kind::f16 (fp16 x fp16 -> fp32) into a
-//               second TMEM double buffer.
+//   warp 1      S issuer (one thread): S_j = Q K_j^T with tcgen05.mma
+//               kind::i8 into a TMEM double buffer.
 //   warps 2-5   softmax: thread = query row = TMEM lane.  Reads S_j with
 //               tcgen05.ld, keeps the running max, writes P_j (fp16) into
-//               shared memory in the 128B-swizzled K-major layout the MMA
-//               reads.  O accumulates in TMEM; the P.V MMA has N = 80, the
+//               an NP-deep ring of shared-memory tiles in the 128B-swizzled
+//               K-major layout the MMA reads.
+//   warp 6      P.V issuer (one thread): O += P_j V_j with kind::f16
+//               (fp16 x fp16 -> fp32 in TMEM).  The MMA has N = 80, the
 //               extra 16 B columns being ones, so O's columns 64..79 carry
 //               the softmax denominator sum(P) at no CUDA-core cost.
+// S and P.V are issued by different threads so that neither waits behind
+// the other: S_{j+2} is issued as soon as the softmax has read S_j and
+// K_{j+2} has landed, P.V_j as soon as P_j is written.
+// The softmax loop body holds only the full-block path; the first block,
+// a ragged last key block and the (rare) O rescale run out of line, which
+// keeps the hot loop small in the instruction cache (measured: the inline
+// general path cost ~8 % of the kernel time).
 // Every mbarrier wait is bounded (~2 s); on expiry the CTA raises an abort
 // flag, records RESS_STATUS_ATTN_WAIT_TIMEOUT, drains its own in-flight
 // copies and MMAs, frees its tensor memory and exits.
@@ -36,8 +43,9 @@
 namespace ress {
 namespace attn {
 
-constexpr int NT = 192;
+constexpr int NT = 224;
 constexpr int NS = 4;                  // K/V ring stages
+constexpr int NP = 3;                  // P ring stages
 constexpr int Q_BYTES = 128 * 64;      // int8
 constexpr int K_BYTES = 64 * 64;       // int8
 constexpr int V_BYTES = 64 * 64 * 2;   // fp16
@@ -46,8 +54,8 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + Q_BYTES;
 constexpr int OFF_V = OFF_K + NS * K_BYTES;
 constexpr int OFF_P = OFF_V + NS * V_BYTES;
-constexpr int ONES_BYTES = 64 * 64 * 2;  // fp16 ones: the 80-column P.V's row-sum columns
-constexpr int OFF_ONES = OFF_P + 2 * P_BYTES;
+constexpr int ONES_BYTES = 16 * 64 * 2;  // fp16 ones: one K = 16 slice of the P.V's row-sum columns
+constexpr int OFF_ONES = OFF_P + NP * P_BYTES;
 constexpr int SMEM_TILES = OFF_ONES + ONES_BYTES;
 constexpr int SMEM_BYTES = SMEM_TILES + 1024;  // + alignment slack
 constexpr uint32_t TMEM_COLS = 256;            // S[2] (64 each) + O (80), power of two
@@ -189,6 +197,18 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// (x0, x1) = (a0, a1) * c + b: one packed fp32 FMA (fma.rn.f32x2), two lanes per issue slot.
+__device__ __forceinline__ void fma2(float &x0, float &x1, float a0, float a1, float c, float b) {
+    asm("{\n\t.reg .b64 ra, rc, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rc, {%4, %4};\n\t"
+        "mov.b64 rb, {%5, %5};\n\t"
+        "fma.rn.f32x2 rd, ra, rc, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(x0), "=f"(x1)
+        : "f"(a0), "f"(a1), "f"(c), "f"(b));
+}
+
 // UMMA shared-memory descriptor (sm100 format: version 1 at bits 46-47,
 // layout type at bits 61-63: 2 = 128B swizzle, 4 = 64B swizzle).
 __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
@@ -209,11 +229,99 @@ constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) <
 //   P.V uses N = 80: the 16 extra B columns are ones, so O columns 64..79 hold sum(P).
 constexpr uint32_t IDESC_F16 = (1u << 4) | (1u << 16) | ((80u >> 3) << 17) | ((128u >> 4) << 24);
 
+// ------------------------------------------------------------- softmax pieces
+// Constants of the S read-out: S arrives as int32 in TMEM; adding MAGIC_I
+// gives the float bits of (1.5 * 2^23 + s), exact for |s| < 2^22 (|s| <=
+// 64 * 127^2), so the scale-and-subtract of the softmax is one FMA.
+constexpr float MAGIC_F = 12582912.0f;
+constexpr uint32_t MAGIC_I = 0x4B400000u;
+
+// Per-thread softmax state handed to the out-of-line paths.
+struct RowCtx {
+    uint32_t tS, tO, lane_addr, sP, prow, rsw;
+    uint64_t *o_full;
+    volatile int *abort_flag;
+    int32_t *status;
+};
+
+// Multiplies this thread's row of O (TMEM, 64 output + 16 row-sum columns)
+// by alpha.  Out of line: rescales are rare after the first few blocks.
+__device__ __noinline__ void rescale_o(uint32_t tO, uint32_t lane_addr, float alpha) {
+#pragma unroll 1
+    for (int ch = 0; ch < O_COLS / 16; ++ch) {
+        uint32_t o16[16];
+        tmem_ld16(tO + ch * 16 + lane_addr, o16);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) o16[t] = __float_as_uint(__uint_as_float(o16[t]) * alpha);
+        tmem_st16(tO + ch * 16 + lane_addr, o16);
+    }
+    tmem_wait_st();
+}
+
+// Writes P = 2^(c*s + bias) for the first nvalid columns (0 beyond) of this
+// thread's row into the P tile at pbase (fp16, 128B-swizzled K-major).
+__device__ __forceinline__ void store_p_masked(const uint32_t (&sv)[64], int nvalid, float c, float bias,
+                                               uint32_t pbase, uint32_t rsw) {
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+        uint32_t h[4];
+#pragma unroll
+        for (int t = 0; t < 8; t += 2) {
+            const int i0 = ch * 8 + t;
+            float x0, x1;
+            fma2(x0, x1, __uint_as_float(sv[i0]), __uint_as_float(sv[i0 + 1]), c, bias);
+            x0 = i0 < nvalid ? x0 : -INFINITY;
+            x1 = i0 + 1 < nvalid ? x1 : -INFINITY;
+            __half2 hp = __floats2half2_rn(ex2(x0), ex2(x1));
+            h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
+        }
+        const uint32_t a = pbase + (((uint32_t)ch ^ rsw) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+                     : "memory");
+    }
+}
+
+// The general softmax step for block j: any number of valid columns, the
+// first block (running maximum not yet set), lazy rescale.  Reads S from
+// TMEM buffer sb itself (the caller has waited for it) and releases it.
+// Out of line so that the hot loop holds only the full-block path.
+// Returns false when a bounded wait failed.
+__device__ __noinline__ bool softmax_block_general(const RowCtx &rc, int j, int sb, int pb, int nvalid, float c,
+                                                   float &m, uint64_t *s_free) {
+    uint32_t sv[64];
+    tmem_ld32(rc.tS + sb * 64 + rc.lane_addr, sv);
+    tmem_ld32(rc.tS + sb * 64 + 32 + rc.lane_addr, sv + 32);
+    tmem_wait_ld();
+    fence_before();
+    mbar_arrive(s_free);
+    float fmx = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < 64; ++t) {
+        sv[t] += MAGIC_I;
+        if (t < nvalid) fmx = fmaxf(fmx, __uint_as_float(sv[t]));
+    }
+    const float mx = c * (fmx - MAGIC_F);
+    const bool grow = mx > m + RESCALE_THRESH;
+    const float m_new = grow ? mx : m;
+    if (__any_sync(0xffffffffu, grow && j > 0)) {
+        const int pj = j - 1;
+        if (!wait_bar_warp(&rc.o_full[pj % NP], (pj / NP) & 1, rc.abort_flag, rc.status)) return false;
+        fence_after();
+        rescale_o(rc.tO, rc.lane_addr, grow ? ex2(m - m_new) : 1.0f);
+    }
+    m = m_new;
+    if (j >= NP && !wait_bar_warp(&rc.o_full[pb], ((j - NP) / NP) & 1, rc.abort_flag, rc.status)) return false;
+    store_p_masked(sv, nvalid, c, fmaf(-c, MAGIC_F, -m), rc.sP + pb * P_BYTES + rc.prow, rc.rsw);
+    fence_before();
+    return true;
+}
+
 struct Bars {
     uint64_t q_full;
     uint64_t kv_full[NS], kv_empty[NS];
-    uint64_t s_full[2], s_free[2], p_full[2], o_full[2];
-    uint64_t mma_done;
+    uint64_t s_full[2], s_free[2], p_full[NP], o_full[NP];
+    uint64_t s_done, pv_done;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -254,10 +362,13 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         for (int i = 0; i < 2; ++i) {
             mbar_init(&B.s_full[i], 1);
             mbar_init(&B.s_free[i], 128);
+        }
+        for (int i = 0; i < NP; ++i) {
             mbar_init(&B.p_full[i], 128);
             mbar_init(&B.o_full[i], 1);
         }
-        mbar_init(&B.mma_done, 1);
+        mbar_init(&B.s_done, 1);
+        mbar_init(&B.pv_done, 1);
         B.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -305,26 +416,9 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+        // ------------------------------------------------------------ S issuer
         if (lane == 0 && cnt > 0) {
             bool ok = wait_bar(&B.q_full, 0, abort_flag, status);
-            auto issue_pv = [&](int i) -> bool {
-                const int pb = i & 1;
-                if (!wait_bar(&B.p_full[pb], (i >> 1) & 1, abort_flag, status)) return false;
-                fence_after();
-                const uint32_t pa = sP + pb * P_BYTES;
-                const uint32_t va = sV + (i % NS) * V_BYTES;
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t ad = make_desc(pa + kk * 32, 16, 1024, LAYOUT_SW128);
-                    // B = [V tile | ones tile]: the second 128B-wide atom along N sits LBO bytes on
-                    const uint64_t bd = make_desc(va + kk * 2048, sOnes - va, 1024, LAYOUT_SW128);
-                    mma_f16(tO, ad, bd, IDESC_F16, (i > 0 || kk > 0) ? 1u : 0u);
-                }
-                mma_commit(&B.o_full[pb]);
-                mma_commit(&B.kv_empty[i % NS]);
-                return true;
-            };
             for (int j = 0; ok && j < cnt; ++j) {
                 const int st = j % NS, sb = j & 1;
                 if (!wait_bar(&B.kv_full[st], (j / NS) & 1, abort_flag, status)) break;
@@ -337,12 +431,40 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                     mma_i8(tS + sb * 64, ad, bd, IDESC_I8, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&B.s_full[sb]);
-                if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
-                if (j == cnt - 1 && !issue_pv(j)) { ok = false; break; }
             }
-            // all MMAs issued by this thread complete before TMEM is freed
-            mma_commit(&B.mma_done);
-            const uint32_t addr = smem_u32(&B.mma_done);
+            // every MMA this thread issued completes before TMEM is freed
+            mma_commit(&B.s_done);
+            const uint32_t addr = smem_u32(&B.s_done);
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(addr, 0) && globaltimer() - t0 < TIMEOUT_NS) {
+            }
+        }
+    } else if (warp == 6) {
+        // ------------------------------------------------------------ P.V issuer
+        if (lane == 0 && cnt > 0) {
+            for (int j = 0; j < cnt; ++j) {
+                const int pb = j % NP, st = j % NS;
+                if (!wait_bar(&B.p_full[pb], (j / NP) & 1, abort_flag, status)) break;
+                // V_j landed (already observed by the S issuer; re-checked here so that
+                // this thread itself orders the tensor core's read after the copy)
+                if (!wait_bar(&B.kv_full[st], (j / NS) & 1, abort_flag, status)) break;
+                fence_after();
+                const uint32_t pa = sP + pb * P_BYTES;
+                const uint32_t va = sV + st * V_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t ad = make_desc(pa + kk * 32, 16, 1024, LAYOUT_SW128);
+                    // B = [V tile | ones]: the second 128B-wide atom along N sits LBO bytes
+                    // past the first; every K slice reads the same 16-row ones tile
+                    const uint32_t vk = va + kk * 2048;
+                    const uint64_t bd = make_desc(vk, sOnes - vk, 1024, LAYOUT_SW128);
+                    mma_f16(tO, ad, bd, IDESC_F16, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&B.o_full[pb]);
+                mma_commit(&B.kv_empty[st]);
+            }
+            mma_commit(&B.pv_done);
+            const uint32_t addr = smem_u32(&B.pv_done);
             const uint64_t t0 = globaltimer();
             while (!mbar_try_wait(addr, 0) && globaltimer() - t0 < TIMEOUT_NS) {
             }
@@ -359,96 +481,85 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         const int r = quad * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const float qs = qscale[(size_t)bh * nqb + qb];
-        const float MAGIC_F = 12582912.0f;
-        const uint32_t MAGIC_I = 0x4B400000u;
         float m = -INFINITY;
         bool ok = true;
         const uint32_t prow = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
         const uint32_t rsw = (uint32_t)(r & 7);
+        const RowCtx rc{tS, tO, lane_addr, sP, prow, rsw, B.o_full, abort_flag, status};
+        const float *ksc = kscale + (size_t)bh * nkb;
+        // two-deep prefetch: block j+2's index and block j+1's scale are
+        // loaded one iteration before they are needed
+        int kb_cur = cnt > 0 ? lst[0] : 0;
+        int kb_nxt = cnt > 1 ? lst[1] : 0;
+        float ks_cur = cnt > 0 ? ksc[kb_cur] : 0.0f;
         for (int j = 0; j < cnt; ++j) {
-            const int sb = j & 1;
-            const int kb = lst[j];
-            const float c = qs * kscale[(size_t)bh * nkb + kb] * sm_scale_log2;
+            const int sb = j & 1, pb = j % NP;
+            const int kb = kb_cur;
+            const float c = qs * ks_cur * sm_scale_log2;
+            ks_cur = (j + 1 < cnt) ? ksc[kb_nxt] : 0.0f;
+            kb_cur = kb_nxt;
+            kb_nxt = (j + 2 < cnt) ? lst[j + 2] : 0;
             const int nvalid = min(64, Tk - kb * 64);
             if (!wait_bar_warp(&B.s_full[sb], (j >> 1) & 1, abort_flag, status)) { ok = false; break; }
             fence_after();
-            uint32_t sv[64];
-            tmem_ld32(tS + sb * 64 + lane_addr, sv);
-            tmem_ld32(tS + sb * 64 + 32 + lane_addr, sv + 32);
-            tmem_wait_ld();
-            fence_before();
-            mbar_arrive(&B.s_free[sb]);
-            float fmx;
-            if (nvalid == 64) {
-                float a0 = -INFINITY, a1 = -INFINITY;
+            if (j == 0 || nvalid < 64) {
+                if (!softmax_block_general(rc, j, sb, pb, nvalid, c, m, &B.s_free[sb])) { ok = false; break; }
+            } else {
+                // hot path: a full block after the first
+                uint32_t sv[64];
+                tmem_ld32(tS + sb * 64 + lane_addr, sv);
+                tmem_ld32(tS + sb * 64 + 32 + lane_addr, sv + 32);
+                tmem_wait_ld();
+                fence_before();
+                mbar_arrive(&B.s_free[sb]);
+                float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-                for (int t = 0; t < 64; t += 4) {
-                    sv[t] += MAGIC_I;
-                    sv[t + 1] += MAGIC_I;
-                    sv[t + 2] += MAGIC_I;
-                    sv[t + 3] += MAGIC_I;
+                for (int t = 0; t < 64; t += 8) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) sv[t + u] += MAGIC_I;
                     a0 = max3(a0, __uint_as_float(sv[t]), __uint_as_float(sv[t + 1]));
                     a1 = max3(a1, __uint_as_float(sv[t + 2]), __uint_as_float(sv[t + 3]));
+                    a2 = max3(a2, __uint_as_float(sv[t + 4]), __uint_as_float(sv[t + 5]));
+                    a3 = max3(a3, __uint_as_float(sv[t + 6]), __uint_as_float(sv[t + 7]));
                 }
-                fmx = fmaxf(a0, a1);
-            } else {
-                fmx = -INFINITY;
-#pragma unroll
-                for (int t = 0; t < 64; ++t) {
-                    sv[t] += MAGIC_I;
-                    if (t < nvalid) fmx = fmaxf(fmx, __uint_as_float(sv[t]));
+                const float mx = c * (max3(a0, a1, fmaxf(a2, a3)) - MAGIC_F);
+                // lazy rescale: the maximum moves only when it grew by more than the threshold
+                const bool grow = mx > m + RESCALE_THRESH;
+                if (__any_sync(0xffffffffu, grow)) {
+                    const float m_new = grow ? mx : m;
+                    const int pj = j - 1;
+                    if (!wait_bar_warp(&B.o_full[pj % NP], (pj / NP) & 1, abort_flag, status)) { ok = false; break; }
+                    fence_after();
+                    rescale_o(tO, lane_addr, ex2(m - m_new));
+                    m = m_new;
                 }
-            }
-            const float mx = c * (fmx - MAGIC_F);
-            // lazy rescale: keep the old maximum unless it grew by more than the threshold
-            const bool grow = mx > m + RESCALE_THRESH;
-            const float m_new = grow ? mx : m;
-            const float alpha = grow ? ex2(m - m_new) : 1.0f;
-            if (__any_sync(0xffffffffu, grow && j > 0)) {
-                // O holds P.V of blocks < j in units of m: wait for the last of them, rescale in TMEM
-                if (!wait_bar_warp(&B.o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, status)) { ok = false; break; }
-                fence_after();
+                // P_{j-NP} (same shared tile) must have been consumed by its P.V
+                if (j >= NP && !wait_bar_warp(&B.o_full[pb], ((j - NP) / NP) & 1, abort_flag, status)) { ok = false; break; }
+                const uint32_t pbase = sP + pb * P_BYTES + prow;
+                const float bias = fmaf(-c, MAGIC_F, -m);
 #pragma unroll
-                for (int ch = 0; ch < O_COLS / 16; ++ch) {
-                    uint32_t o16[16];
-                    tmem_ld16(tO + ch * 16 + lane_addr, o16);
-                    tmem_wait_ld();
+                for (int ch = 0; ch < 8; ++ch) {
+                    uint32_t h[4];
 #pragma unroll
-                    for (int t = 0; t < 16; ++t) o16[t] = __float_as_uint(__uint_as_float(o16[t]) * alpha);
-                    tmem_st16(tO + ch * 16 + lane_addr, o16);
-                }
-                tmem_wait_st();
-            }
-            // P_{j-2} (same shared buffer) must have been consumed by its P.V
-            if (j >= 2 && !wait_bar_warp(&B.o_full[sb], ((j - 2) >> 1) & 1, abort_flag, status)) { ok = false; break; }
-            const float bias = fmaf(-c, MAGIC_F, -m_new);
-            const uint32_t pbase = sP + sb * P_BYTES + prow;
-#pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-                uint32_t h[4];
-#pragma unroll
-                for (int t = 0; t < 8; t += 2) {
-                    const int i0 = ch * 8 + t;
-                    float p0 = ex2(fmaf(c, __uint_as_float(sv[i0]), bias));
-                    float p1 = ex2(fmaf(c, __uint_as_float(sv[i0 + 1]), bias));
-                    if (nvalid < 64) {
-                        p0 = i0 < nvalid ? p0 : 0.0f;
-                        p1 = i0 + 1 < nvalid ? p1 : 0.0f;
+                    for (int t = 0; t < 8; t += 2) {
+                        const int i0 = ch * 8 + t;
+                        float x0, x1;
+                        fma2(x0, x1, __uint_as_float(sv[i0]), __uint_as_float(sv[i0 + 1]), c, bias);
+                        __half2 hp = __floats2half2_rn(ex2(x0), ex2(x1));
+                        h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
                     }
-                    __half2 hp = __floats2half2_rn(p0, p1);
-                    h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
+                    const uint32_t a = pbase + (((uint32_t)ch ^ rsw) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]),
+                                 "r"(h[3])
+                                 : "memory");
                 }
-                const uint32_t a = pbase + (((uint32_t)ch ^ rsw) << 4);
-                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
-                             : "memory");
+                fence_before();
             }
-            fence_before();
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&B.p_full[sb]);
-            m = m_new;
+            mbar_arrive(&B.p_full[pb]);
         }
         if (ok && cnt > 0) {
-            ok = wait_bar_warp(&B.o_full[(cnt - 1) & 1], ((cnt - 1) >> 1) & 1, abort_flag, status);
+            ok = wait_bar_warp(&B.o_full[(cnt - 1) % NP], ((cnt - 1) / NP) & 1, abort_flag, status);
             fence_after();
         }
         const int t = qb * 128 + r;
