@@ -561,7 +561,7 @@ __device__ __forceinline__ void vb_row(const uint16_t *vb, int k, float *v) {
 // round-to-nearest, so this equals the sparse sum over the dropped entries
 // (the oracle's order) while letting the loads pipeline.
 __device__ void g_drift(GroupScratch &S, const float *P, float *Pd, const uint8_t *drop, const uint16_t *vb,
-                        const float *M, int n_cand, int g, int t) {
+                        const float *Mt, int n_cand, int g, int t) {
     for (int k = t; k < n_cand; k += G_NT) Pd[k] = drop[k] ? P[k] : 0.0f;
     gbar(g);
     float acc = 0.0f, sp = 0.0f;
@@ -588,7 +588,7 @@ __device__ void g_drift(GroupScratch &S, const float *P, float *Pd, const uint8_
     gbar(g);
     float mg = 0.0f;
 #pragma unroll 16
-    for (int j = 0; j < HD; ++j) mg = __fmaf_rn(M[t * HD + j], S.g[j], mg);
+    for (int j = 0; j < HD; ++j) mg = __fmaf_rn(Mt[j * HD + t], S.g[j], mg);
     S.Mg[t] = mg;
     gbar(g);
     if (t == 0) {
@@ -624,7 +624,8 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
             const int k = i >> 3, c = i & 7;
             dst[k * 8 + (c ^ (k & 7))] = src[i];
         }
-        for (int i = threadIdx.x; i < HD * HD; i += blockDim.x) M[i] = Mg_in[(size_t)h * HD * HD + i];
+        // M transposed: thread t then reads M[t][j] at Mt[j * HD + t], one bank per lane
+        for (int i = threadIdx.x; i < HD * HD; i += blockDim.x) M[(i & (HD - 1)) * HD + (i >> 6)] = Mg_in[(size_t)h * HD * HD + i];
     }
     __syncthreads();
     const int g = threadIdx.x / G_NT, t = threadIdx.x % G_NT;
@@ -670,7 +671,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     {
         float acc = 0.0f;
 #pragma unroll 8
-        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(bf16r(M[t * HD + j]), S.vq[j], acc);
+        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(bf16r(M[j * HD + t]), S.vq[j], acc);
         S.Mvq[t] = bf16r(acc);
     }
     gbar(g);
@@ -726,12 +727,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
             for (int k = t; k < n_cand; k += G_NT) best[k] = drop[k];
         const float G = S.G, K = S.K, tqb = S.tqb;
         int nd = 0, nk = 0, ben = 0;
-        for (int k = t; k < n_cand; k += G_NT) {
-            float v[HD];
-            vb_row(vb, k, v);
-            float acc = 0.0f;
-#pragma unroll
-            for (int j = 0; j < HD; ++j) acc = __fmaf_rn(v[j], S.Mgb[j], acc);
+        auto quality = [&](int k, float acc) {
             const float tkk = bf16r(acc);
             const float r = bf16r(__fmul_rn(P[k], bf16r(__fsub_rn(tkk, tqb))));
             if (drop[k]) {
@@ -744,6 +740,30 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
                 ++nk;
             }
             valid[k] = drop[k] ? 0 : 1;
+        };
+        // two candidates per step: two independent FMA chains in flight
+        int k = t;
+        for (; k + G_NT < n_cand; k += 2 * G_NT) {
+            float v0[HD], v1[HD];
+            vb_row(vb, k, v0);
+            vb_row(vb, k + G_NT, v1);
+            float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < HD; ++j) {
+                const float mj = S.Mgb[j];
+                a0 = __fmaf_rn(v0[j], mj, a0);
+                a1 = __fmaf_rn(v1[j], mj, a1);
+            }
+            quality(k, a0);
+            quality(k + G_NT, a1);
+        }
+        if (k < n_cand) {
+            float v0[HD];
+            vb_row(vb, k, v0);
+            float a0 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < HD; ++j) a0 = __fmaf_rn(v0[j], S.Mgb[j], a0);
+            quality(k, a0);
         }
         const int n_drop = gsum(nd, S.red, g, t);
         const int n_kept = gsum(nk, S.red, g, t);
