@@ -32,6 +32,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 N_FRAMES = 32
+# DRAM bytes (read + write) of one attention launch on the 32-frame layer:
+# 237.4 MB measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) on
+# the 24-frame layer, scaled by the token count 43,968 / 32,976.
+ATTN_DRAM_BYTES_PER_LAUNCH = 237.4e6 * 43968 / 32976
 SPARSE_RATIO = 0.5
 CDF = 0.97
 METRIC = "global-attn layer throughput, VGGT cfg2 (32 views, 43,968 tokens, 16x64 heads, apply_ress sr=0.5)"
@@ -397,7 +401,9 @@ def run_ress(args):
             "gpu_launches": 10 * args.steps,
             "roofline": {"bound": "tensor", "kernel": "sparse_attn_kernel", "achieved": achieved,
                          "peak": mixed_peak, "unit": "TFLOP/s", "frac": achieved / mixed_peak,
-                         "traffic": None, "attn_ms": attn_ms, "attn_tflop_per_launch": attn_flops / 1e12,
+                         "traffic": ATTN_DRAM_BYTES_PER_LAUNCH * args.frames / N_FRAMES,
+                         "traffic_note": "dram read+write bytes per launch, ncu on the 24-frame layer scaled by tokens",
+                         "attn_ms": attn_ms, "attn_tflop_per_launch": attn_flops / 1e12,
                          "peak_note": f"{peak_src}: harmonic mix of bf16 burst {bf16_peak:.0f} TF/s (PV half) and "
                                       "int8 = 2x bf16 (QK half)"},
             "clocks": clk.summary(),

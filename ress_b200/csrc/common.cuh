@@ -21,9 +21,10 @@ constexpr int KS_K = 64;    // key block (attention.py:38-39)
 
 // Raise a kernel's dynamic shared-memory limit once per (device, kernel,
 // size): the attribute sticks to the function in a device's context, so
-// later launches skip the driver call.
+// later launches skip the driver call.  Set for any dynamic size: the 48 KB
+// default covers static plus dynamic shared memory together.
 inline void set_smem_attr(const void *kern, size_t bytes) {
-    if (bytes <= 48 * 1024) return;
+    if (bytes == 0) return;
     int dev = 0;
     cudaGetDevice(&dev);
     static thread_local const void *last_k[64] = {nullptr};
@@ -194,9 +195,17 @@ __device__ void block_select_top_m(const uint32_t *key, const uint8_t *valid, in
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int b = tid; b < 256; b += NT) sc.hist[b] = 0;
         __syncthreads();
-        for (int i = i0; i < i1; ++i) {
-            uint32_t k = key[i];
-            if (valid[i] && (k & pmask) == prefix) atomicAdd(&sc.hist[(k >> shift) & 255u], 1);
+        // warp-aggregated histogram: lanes holding the same digit add once
+        // (every thread runs the same trip count, so the warp stays converged)
+        for (int j = 0; j < chunk; ++j) {
+            const int i = i0 + j;
+            int bin = -1;
+            if (i < i1) {
+                const uint32_t k = key[i];
+                if (valid[i] && (k & pmask) == prefix) bin = (int)((k >> shift) & 255u);
+            }
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (bin >= 0 && (tid & 31) == __ffs(peers) - 1) atomicAdd(&sc.hist[bin], __popc(peers));
         }
         __syncthreads();
         // find the bin b with count(> b) < rem <= count(>= b), scanning from 255 down

@@ -92,7 +92,7 @@ __global__ void vbar_terms_kernel(const T *__restrict__ vbar, const float *__res
 // ----------------------------------------------------------------- restore-swap
 struct RSShared {
     SelectScratch sc;
-    float M[HD * HD];
+    float Mt[HD * HD];  // M transposed: thread t reads M[t][j] at Mt[j * HD + t], one bank per lane
     float vq[HD], Mvq[HD], g[HD], Mg[HD], Mgb[HD];
     float tm, sum_pd, G, K, J, bestJ, tqb, tqs;
     int flag;
@@ -112,40 +112,90 @@ __device__ __forceinline__ void load_row64(const uint16_t *src, float *v) {
     }
 }
 
-// g, Mg, G = ||g||^2_M and K for the current drop set (projected.py:868-878,
-// 908-920).  vb: bf16 bits (nkp, 64) of this head.
-__device__ void rs_drift(RSShared &S, const float *P, const uint8_t *drop, const uint16_t *vb,
-                         int n_cand) {
+// Rows of vbar per shared-memory stage of the drift chains (two stages,
+// filled with cp.async while the previous one is consumed).
+constexpr int DCH = 64;
+constexpr int STAGE_BYTES = 2 * DCH * HD * 2;
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// acc[d] = sum_k w(k) * vbar[k][d] for d = tid < 64 as one sequential fp32
+// FMA chain per dimension in k order (with w(k) = +0 for masked entries,
+// which leaves the chain bit-for-bit unchanged: it starts at +0 and never
+// reaches -0), and total = sequential fp32 sum of w(k) (thread 64).  vbar
+// rows stream through two shared-memory stages of DCH rows loaded by the
+// whole CTA with cp.async.  mask == nullptr: w(k) = P[k] for all n entries.
+__device__ void rs_chain(const float *P, const uint8_t *mask, const uint16_t *vb, int n, uint16_t *stage,
+                         float &acc_out, float &total_out) {
     const int tid = threadIdx.x;
-    if (tid < HD) {
-        float acc = 0.0f;
-        int k = 0;
-        for (; k + 4 <= n_cand; k += 4) {
-            float v0 = bf16_from_bits(vb[(size_t)(k + 0) * HD + tid]);
-            float v1 = bf16_from_bits(vb[(size_t)(k + 1) * HD + tid]);
-            float v2 = bf16_from_bits(vb[(size_t)(k + 2) * HD + tid]);
-            float v3 = bf16_from_bits(vb[(size_t)(k + 3) * HD + tid]);
-            if (drop[k + 0]) acc = __fmaf_rn(P[k + 0], v0, acc);
-            if (drop[k + 1]) acc = __fmaf_rn(P[k + 1], v1, acc);
-            if (drop[k + 2]) acc = __fmaf_rn(P[k + 2], v2, acc);
-            if (drop[k + 3]) acc = __fmaf_rn(P[k + 3], v3, acc);
+    const int nch = (n + DCH - 1) / DCH;
+    auto issue = [&](int c) {
+        const int r0 = c * DCH, rows = min(DCH, n - r0);
+        uint16_t *dst = stage + (c & 1) * DCH * HD;
+        for (int i = tid; i < rows * 8; i += SEL_NT)
+            cp_async16(dst + i * 8, vb + (size_t)r0 * HD + (size_t)i * 8);
+    };
+    float acc = 0.0f, tot = 0.0f;
+    issue(0);
+    cp_async_commit();
+    for (int c = 0; c < nch; ++c) {
+        if (c + 1 < nch) issue(c + 1);
+        cp_async_commit();
+        cp_async_wait1();
+        __syncthreads();
+        const int r0 = c * DCH, rows = min(DCH, n - r0);
+        const uint16_t *st = stage + (c & 1) * DCH * HD;
+        if (tid < HD) {
+            int r = 0;
+            for (; r + 8 <= rows; r += 8) {
+                float w[8], v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int k = r0 + r + u;
+                    w[u] = (mask == nullptr || mask[k]) ? P[k] : 0.0f;
+                    v[u] = bf16_from_bits(st[(r + u) * HD + tid]);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc = __fmaf_rn(w[u], v[u], acc);
+            }
+            for (; r < rows; ++r) {
+                const int k = r0 + r;
+                acc = __fmaf_rn((mask == nullptr || mask[k]) ? P[k] : 0.0f, bf16_from_bits(st[r * HD + tid]), acc);
+            }
+        } else if (tid == HD) {
+            for (int r = 0; r < rows; ++r) {
+                const int k = r0 + r;
+                tot = __fadd_rn(tot, (mask == nullptr || mask[k]) ? P[k] : 0.0f);
+            }
         }
-        for (; k < n_cand; ++k)
-            if (drop[k]) acc = __fmaf_rn(P[k], bf16_from_bits(vb[(size_t)k * HD + tid]), acc);
-        S.g[tid] = bf16r(acc);  // masked_vbar_d, finished below
-    } else if (tid == HD) {
-        float s = 0.0f;
-        for (int k = 0; k < n_cand; ++k) s = __fadd_rn(s, drop[k] ? P[k] : 0.0f);
-        S.sum_pd = bf16r(s);
+        __syncthreads();
     }
+    acc_out = acc;
+    total_out = tot;
+}
+
+// g, Mg, G = ||g||^2_M and K for the current drop set (projected.py:868-878,
+// 908-920).  vb: bf16 bits (nkp, 64) of this head.  S.Mt holds M transposed.
+__device__ void rs_drift(RSShared &S, const float *P, const uint8_t *drop, const uint16_t *vb,
+                         int n_cand, uint16_t *stage) {
+    const int tid = threadIdx.x;
+    float acc, tot;
+    rs_chain(P, drop, vb, n_cand, stage, acc, tot);
+    if (tid < HD) S.g[tid] = bf16r(acc);  // masked_vbar_d, finished below
+    else if (tid == HD) S.sum_pd = bf16r(tot);
     __syncthreads();
     if (tid < HD) S.g[tid] = __fsub_rn(__fmul_rn(S.sum_pd, S.vq[tid]), S.g[tid]);
     __syncthreads();
     if (tid < HD) {
-        float acc = 0.0f;
+        float a = 0.0f;
 #pragma unroll 8
-        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(S.M[tid * HD + j], S.g[j], acc);
-        S.Mg[tid] = acc;
+        for (int j = 0; j < HD; ++j) a = __fmaf_rn(S.Mt[j * HD + tid], S.g[j], a);
+        S.Mg[tid] = a;
     }
     __syncthreads();
     if (tid == 0) {
@@ -170,10 +220,10 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     const int row = blockIdx.x;
     const int bh = row / nq, h = bh % H;
     const int tid = threadIdx.x;
-    float *P = reinterpret_cast<float *>(dyn);                 // nkp
+    uint16_t *stage = reinterpret_cast<uint16_t *>(dyn);       // 2 x DCH x 64 bf16
+    float *P = reinterpret_cast<float *>(dyn + STAGE_BYTES);   // nkp
     float *ssq = P + nkp;                                      // n_cand
-    float *raw = ssq + n_cand;                                 // n_cand
-    uint32_t *key = reinterpret_cast<uint32_t *>(raw + n_cand); // n_cand
+    uint32_t *key = reinterpret_cast<uint32_t *>(ssq + n_cand); // n_cand
     uint8_t *drop = reinterpret_cast<uint8_t *>(key + n_cand);   // n_cand each
     uint8_t *best = drop + n_cand;
     uint8_t *valid = best + n_cand;
@@ -181,24 +231,21 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     uint8_t *sel2 = sel + n_cand;
     const uint16_t *vb = vb16 + (size_t)bh * nkp * HD;
 
-    for (int i = tid; i < HD * HD; i += SEL_NT) S.M[i] = M[(size_t)h * HD * HD + i];
+    for (int i = tid; i < HD * HD; i += SEL_NT) S.Mt[(i & (HD - 1)) * HD + (i >> 6)] = M[(size_t)h * HD * HD + i];
     for (int k = tid; k < nkp; k += SEL_NT) P[k] = bf16r(DT<T>::load(attn, (size_t)row * nkp + k));
     __syncthreads();
     // dense_reference over all pooled blocks: v_bar_query = P @ v_bar, total = sum(P)
-    if (tid < HD) {
-        float acc = 0.0f;
-        for (int k = 0; k < nkp; ++k) acc = __fmaf_rn(P[k], bf16_from_bits(vb[(size_t)k * HD + tid]), acc);
-        S.vq[tid] = bf16r(acc);
-    } else if (tid == HD) {
-        float s = 0.0f;
-        for (int k = 0; k < nkp; ++k) s = __fadd_rn(s, P[k]);
-        S.tm = bf16r(s);
+    {
+        float acc, tot;
+        rs_chain(P, nullptr, vb, nkp, stage, acc, tot);
+        if (tid < HD) S.vq[tid] = bf16r(acc);
+        else if (tid == HD) S.tm = bf16r(tot);
     }
     __syncthreads();
     if (tid < HD) {
         float acc = 0.0f;
 #pragma unroll 8
-        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(bf16r(S.M[tid * HD + j]), S.vq[j], acc);
+        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(bf16r(S.Mt[j * HD + tid]), S.vq[j], acc);
         S.Mvq[tid] = bf16r(acc);
     }
     __syncthreads();
@@ -235,14 +282,14 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     for (int k = tid; k < n_cand; k += SEL_NT) drop[k] = sel[k] ? 0 : 1;
     __syncthreads();
     if (track_best) {
-        rs_drift(S, P, drop, vb, n_cand);
+        rs_drift(S, P, drop, vb, n_cand, stage);
         if (tid == 0) S.bestJ = S.J;
         for (int k = tid; k < n_cand; k += SEL_NT) best[k] = drop[k];
         __syncthreads();
     }
     for (int it = 0; it < n_iters; ++it) {
         const int pic = (int)rintf(__fmul_rn(fr.f[it], (float)nt));
-        rs_drift(S, P, drop, vb, n_cand);
+        rs_drift(S, P, drop, vb, n_cand, stage);
         if (tid == 0) {
             S.flag = (track_best && S.J < S.bestJ) ? 1 : 0;
             if (S.flag) S.bestJ = S.J;
@@ -264,7 +311,6 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
             for (int j = 0; j < HD; ++j) acc = __fmaf_rn(v[j], S.Mgb[j], acc);
             float tkk = bf16r(acc);
             float r = bf16r(__fmul_rn(P[k], bf16r(__fsub_rn(tkk, tqb))));
-            raw[k] = r;
             if (drop[k]) {
                 float rq = knorm_quality(G, K, __fadd_rn(__fmul_rn(2.0f, r), ssq[k]), P[k]);
                 key[k] = order_key(rq);
@@ -291,7 +337,7 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
         __syncthreads();
     }
     if (track_best) {
-        rs_drift(S, P, drop, vb, n_cand);
+        rs_drift(S, P, drop, vb, n_cand, stage);
         const bool keep_final = S.J < S.bestJ;
         if (!keep_final)
             for (int k = tid; k < n_cand; k += SEL_NT) drop[k] = best[k];
@@ -818,7 +864,7 @@ static size_t rs2_row_bytes(int nkp, int n_cand) {
 }
 
 static size_t rs_smem(int nkp, int n_cand) {
-    return (size_t)nkp * 4 + (size_t)n_cand * (4 + 4 + 4 + 5);
+    return (size_t)STAGE_BYTES + (size_t)nkp * 4 + (size_t)n_cand * (4 + 4 + 5);
 }
 
 template <typename T>

@@ -121,6 +121,32 @@ def test_restore_swap_bit_exact(shape, dtype, sr):
     K.check_status()
 
 
+def test_restore_swap_large_layer_bit_exact():
+    """60 frames: 1,283 candidate blocks, past the size at which a head's pooled
+    V stays resident in shared memory, so the kernel that streams it through
+    shared-memory stages runs.  Two heads keep the oracle quick."""
+    shape = synth.LayerShape(n_frames=60)
+    H = 2
+    q, k, v = (t[:, :H].contiguous() for t in synth.layer_qkv(shape, seed=3, dtype=torch.bfloat16, device="cuda"))
+    L = K.Layout(1, H, shape.n_frames, shape.n_special, shape.hw)
+    assert L.n_cand > 1200
+    qbar, _, _ = K.pool_quant_q(q, L, quant=False)
+    kbar, vbar, _, _, _, _ = K.pool_quant_kv(k, v, L, quant=False)
+    af, ac = K.predict(qbar, kbar, L.n_cand)
+    hs = synth.fisher_table(seed=1)[0, 0, :H]
+    nts = K.hess_adjust(K.baseline(ac, 0.6).view(1, H, -1), K.scores_norm(hs), L.n_cand, min_clamp=2)
+    M = synth.metric_from_weight(synth.out_proj_weight())[:H].contiguous()
+    r = K.restore_swap(af, vbar, M.cuda(), nts.view(-1), L.n_cand, sink_blocks=L.sink_blocks, want_drop=True,
+                       want_s=True)
+    torch.cuda.synchronize()
+    drop_o, s_o = oracle.restore_swap(af.cpu(), vbar.cpu().to(torch.bfloat16), M, nts.cpu().view(-1), L.n_cand)
+    assert _eq(r["s"], s_o)
+    assert torch.equal(r["drop"].cpu().bool(), drop_o)
+    lists_o, counts_o = oracle.keep_lists(~drop_o, L.sink_blocks)
+    assert torch.equal(r["counts"].cpu(), counts_o)
+    K.check_status()
+
+
 @pytest.mark.parametrize("shape,dtype", CASES)
 def test_select_prob_and_top_m(shape, dtype):
     q, k, v = _inputs(shape, dtype)
