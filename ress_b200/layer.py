@@ -134,6 +134,51 @@ def special_attention(q, k, v, L: K.Layout):
     return F.scaled_dot_product_attention(qs, k, v)
 
 
+def select_blocks(attn_full, attn_cond, vbar, B: int, H: int, nq: int, n_cand: int, sink_blocks: int,
+                  budget: BudgetSpec | None, order: OrderSpec, *, num_to_select=None, budget_fn=None,
+                  lead_blocks: int = 0, shard: HeadShard | None = None, ws=None):
+    """Budget (a.6, a.7) and block order (a.8-a.11) of one layer's (head,
+    q-block) rows -> (nts (B, H, nq) int32, dict(lists, counts)).
+    attn_full (B*H, nq, nkp), attn_cond (B*H, nq, n_cand), vbar (B*H, nkp, 64)."""
+    dev = attn_cond.device
+    min_sel = min(MIN_NUM_TO_SELECT, n_cand)
+    if num_to_select is not None:
+        nts = num_to_select.to(device=dev, dtype=torch.int32).reshape(B, H, nq).clamp(min=min_sel)
+    elif budget is not None:
+        base = K.baseline(attn_cond, budget.sparse_ratio, budget.cdf_threshold).view(B, H, nq)
+        if budget.kind == "hess" and shard is not None:
+            full = shard.gather(base)
+            nts_full = K.hess_adjust(full, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
+            nts = nts_full[:, shard.h0: shard.h0 + H].contiguous()
+        elif budget.kind == "hess":
+            nts = K.hess_adjust(base, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
+        else:
+            nts = base.clamp(min=min_sel)
+    elif budget_fn is not None:
+        nts = budget_fn(attn_cond.view(B, H, nq, n_cand))
+        nts = nts.to(device=dev, dtype=torch.int32).reshape(B, H, nq).clamp(min=min_sel)
+    else:
+        raise AssertionError("num_to_select (or budget_fn) required unless dense=True")
+
+    if order.kind == "restore_swap":
+        r = K.restore_swap(attn_full, vbar, order.M, nts.view(-1), n_cand, n_iters=order.n_iters,
+                           track_best=order.track_best, restore_frac=order.restore_frac, decay=order.decay,
+                           sink_blocks=sink_blocks, lead_blocks=lead_blocks, ws=ws)
+    elif order.kind == "probability":
+        r = K.select_prob(attn_cond, nts.view(-1), sink_blocks=sink_blocks, lead_blocks=lead_blocks)
+    elif order.kind == "random":
+        key = torch.rand(attn_cond.shape, device=dev, dtype=torch.float32, generator=_random_gen(dev))
+        keep = K.top_m_mask(key, nts.view(-1)).view(-1, n_cand)
+        full_map = torch.cat([keep, torch.ones(keep.shape[0], sink_blocks, dtype=torch.bool, device=dev)], -1)
+        if lead_blocks:
+            full_map[:, :lead_blocks] = True
+        lists, counts = K.map_to_lists(full_map)
+        r = dict(lists=lists, counts=counts)
+    else:
+        raise ValueError(order.kind)
+    return nts, r
+
+
 def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSpec, *,
                  num_to_select: torch.Tensor | None = None, budget_fn=None, keep_pooled: bool = False,
                  lead_blocks: int = 0, out: torch.Tensor | None = None,
@@ -163,7 +208,6 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
     kbar, vbar, k8, ks, v16, km = K.pool_quant_kv(k, v, L, ws=ws)
     need_full = order.kind == "restore_swap" or keep_pooled
     attn_full, attn_cond = K.predict(qbar, kbar, n_cand, full=need_full, cond=True)
-    min_sel = min(MIN_NUM_TO_SELECT, n_cand)
     width = n_cand + L.sink_blocks
     if joint_select_fn is not None:
         # one-shot joint selection (attention.py:501-508): the callable returns the final map
@@ -183,40 +227,9 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
             view[:, :, :, : L.special] = x_special.view(B, H, L.frames, L.special, 64).float()
         return LayerResult(out=out, layout=L, lists=lists, counts=counts, nts=None, attn_full=attn_full,
                            attn_cond=attn_cond, vbar=vbar)
-    if num_to_select is not None:
-        nts = num_to_select.to(device=dev, dtype=torch.int32).reshape(B, H, L.nq).clamp(min=min_sel)
-    elif budget is not None:
-        base = K.baseline(attn_cond, budget.sparse_ratio, budget.cdf_threshold).view(B, H, L.nq)
-        if budget.kind == "hess" and shard is not None:
-            full = shard.gather(base)
-            nts_full = K.hess_adjust(full, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
-            nts = nts_full[:, shard.h0: shard.h0 + H].contiguous()
-        elif budget.kind == "hess":
-            nts = K.hess_adjust(base, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
-        else:
-            nts = base.clamp(min=min_sel)
-    elif budget_fn is not None:
-        nts = budget_fn(attn_cond.view(B, H, L.nq, n_cand))
-        nts = nts.to(device=dev, dtype=torch.int32).reshape(B, H, L.nq).clamp(min=min_sel)
-    else:
-        raise AssertionError("num_to_select (or budget_fn) required unless dense=True")
-
-    if order.kind == "restore_swap":
-        r = K.restore_swap(attn_full, vbar, order.M, nts.view(-1), n_cand, n_iters=order.n_iters,
-                           track_best=order.track_best, restore_frac=order.restore_frac, decay=order.decay,
-                           sink_blocks=L.sink_blocks, lead_blocks=lead_blocks, ws=ws)
-    elif order.kind == "probability":
-        r = K.select_prob(attn_cond, nts.view(-1), sink_blocks=L.sink_blocks, lead_blocks=lead_blocks)
-    elif order.kind == "random":
-        key = torch.rand(attn_cond.shape, device=dev, dtype=torch.float32, generator=_random_gen(dev))
-        keep = K.top_m_mask(key, nts.view(-1)).view(-1, n_cand)
-        full_map = torch.cat([keep, torch.ones(keep.shape[0], L.sink_blocks, dtype=torch.bool, device=dev)], -1)
-        if lead_blocks:
-            full_map[:, :lead_blocks] = True
-        lists, counts = K.map_to_lists(full_map)
-        r = dict(lists=lists, counts=counts)
-    else:
-        raise ValueError(order.kind)
+    nts, r = select_blocks(attn_full, attn_cond, vbar, B, H, L.nq, n_cand, L.sink_blocks, budget, order,
+                           num_to_select=num_to_select, budget_fn=budget_fn, lead_blocks=lead_blocks, shard=shard,
+                           ws=ws)
 
     if map_hook is not None:
         fm = K.lists_to_map(r["lists"], r["counts"], width).view(B, H, L.nq, width)

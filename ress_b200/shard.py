@@ -11,6 +11,8 @@ every rank over all heads (it is tiny).  The gather uses the list form of
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 import torch.distributed as dist
 
@@ -36,3 +38,168 @@ def make_gather(world: int, group=None):
 def make_head_shard(n_heads: int, world: int, rank: int, group=None) -> HeadShard:
     h0, _ = head_range(n_heads, world, rank)
     return HeadShard(h0=h0, h_total=n_heads, gather=make_gather(world, group))
+
+
+# ----------------------------------------------------------------- views
+# Whole-model runs with many views shard the frames: rank r owns frames
+# [r * F, (r + 1) * F) of every layer (F = frames / world).  A global layer
+# then needs every key and value, so K and V are all-gathered (the only
+# large exchange), while each rank keeps its own queries.  The pooled-map
+# q-blocks are 128 patch tokens of the global patch order, so a rank's
+# first and last q-block can straddle a shard boundary; the up-to-127 patch
+# queries it lacks come from its neighbours (each rank contributes its first
+# and last 128 patch queries to a small all-gather), and the straddling
+# q-block is computed on both sides, each keeping the rows of its own tokens.
+# Every (head, q-block) row then sees exactly the inputs of the unsharded
+# layer, so its budget, keep list and output are the same bits.
+
+KS_Q = 128
+
+
+@dataclass
+class ViewGeom:
+    """Where rank ``rank`` of ``world`` sits in a layer of ``frames`` frames."""
+
+    frames: int
+    special: int
+    hw: int
+    world: int
+    rank: int
+
+    def __post_init__(self):
+        if self.frames % self.world:
+            raise ValueError(f"{self.frames} frames do not split evenly over {self.world} ranks")
+        if self.frames_local * self.hw < KS_Q:
+            raise ValueError("each rank needs at least one q-block of its own patch tokens")
+
+    @property
+    def frames_local(self) -> int:
+        return self.frames // self.world
+
+    @property
+    def f0(self) -> int:
+        return self.rank * self.frames_local
+
+    @property
+    def p0(self) -> int:
+        """First global patch index of this rank."""
+        return self.f0 * self.hw
+
+    @property
+    def p1(self) -> int:
+        return self.p0 + self.frames_local * self.hw
+
+    @property
+    def Tp(self) -> int:
+        return self.frames * self.hw
+
+    @property
+    def b0(self) -> int:
+        """First global q-block that holds one of this rank's patch tokens."""
+        return self.p0 // KS_Q
+
+    @property
+    def b1(self) -> int:
+        return -(-self.p1 // KS_Q)
+
+    @property
+    def lo(self) -> int:
+        """Patch queries of the previous rank that this rank's first q-block needs."""
+        return self.p0 - self.b0 * KS_Q
+
+    @property
+    def hi(self) -> int:
+        """Patch queries of the next rank that this rank's last q-block needs."""
+        return min(self.b1 * KS_Q, self.Tp) - self.p1
+
+
+def patch_tokens(x: torch.Tensor, special: int, hw: int) -> torch.Tensor:
+    """(B, H, F*(special+hw), 64) full layout -> (B, H, F*hw, 64) patch tokens."""
+    B, H, T, D = x.shape
+    f = T // (special + hw)
+    return x.view(B, H, f, special + hw, D)[:, :, :, special:].reshape(B, H, f * hw, D)
+
+
+def view_exchange_parts(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, geom: ViewGeom) -> dict:
+    """What this rank contributes to the view exchange: its K and V and the
+    first / last 128 patch queries (the neighbours' halos)."""
+    qp = patch_tokens(q, geom.special, geom.hw)
+    return dict(k=k.contiguous(), v=v.contiguous(), qhead=qp[:, :, :KS_Q].contiguous(),
+                qtail=qp[:, :, -KS_Q:].contiguous())
+
+
+def make_view_gather(world: int, group=None):
+    """all_gather over the process group: (name, tensor) -> list of world tensors."""
+    def gather(name: str, t: torch.Tensor):
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t, group=group)
+        return parts
+    return gather
+
+
+def view_assemble(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, geom: ViewGeom, gather) -> tuple:
+    """-> (qp, k_full, v_full): this rank's q-block queries (patch tokens
+    [b0*128, min(b1*128, Tp)) of the global patch order, (B, H, n, 64)) and
+    every key and value in the full token layout.  ``gather(name, t)``
+    returns the list of every rank's ``t`` in rank order (an all-gather)."""
+    mine = view_exchange_parts(q, k, v, geom)
+    k_full = torch.cat(gather("k", mine["k"]), dim=2)
+    v_full = torch.cat(gather("v", mine["v"]), dim=2)
+    heads = gather("qhead", mine["qhead"])
+    tails = gather("qtail", mine["qtail"])
+    pieces = []
+    if geom.lo:
+        pieces.append(tails[geom.rank - 1][:, :, KS_Q - geom.lo:])
+    pieces.append(patch_tokens(q, geom.special, geom.hw))
+    if geom.hi:
+        pieces.append(heads[geom.rank + 1][:, :, : geom.hi])
+    return torch.cat(pieces, dim=2), k_full, v_full
+
+
+@dataclass
+class ViewLayerResult:
+    out: torch.Tensor      # (B, H, F_local*(special+hw), 64) fp32, this rank's tokens
+    lists: torch.Tensor    # (B*H*(b1-b0), width) int32 keep lists of q-blocks b0..b1-1
+    counts: torch.Tensor
+    nts: torch.Tensor      # (B, H, b1-b0) int32 budgets
+    geom: ViewGeom
+
+
+def view_sharded_layer(q, k, v, geom: ViewGeom, budget, order, gather, *, lead_blocks: int = 0) -> ViewLayerResult:
+    """One sparse global-attention layer on this rank's frames.  q, k, v:
+    (B, H, F_local*(special+hw), 64) CUDA, this rank's tokens in the full
+    layout.  Same stages as ``layer.global_layer``; the pooled keys, the
+    int8 keys, their mean and the fp16 values are formed from the gathered
+    full K and V (identically on every rank)."""
+    from . import kernels as K
+    from . import layer as LY
+
+    B, H = q.shape[0], q.shape[1]
+    dev = q.device
+    qp, k_full, v_full = view_assemble(q, k, v, geom, gather)
+    Lk = K.Layout(B, H, geom.frames, geom.special, geom.hw)
+    Lq = K.Layout(B, H, 1, 0, qp.shape[2])
+    Ll = K.Layout(B, H, geom.frames_local, geom.special, geom.hw)
+    ws = K.workspace(dev, B * H, Lk.Tp, Lk.Tk, Lk.n_cand)
+    main = torch.cuda.current_stream(dev)
+    side = LY._side_stream(dev)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        x_special = LY.special_attention(q, k_full, v_full, Ll)
+    for t in (q, k_full, v_full):
+        t.record_stream(side)
+    qbar, q8, qs = K.pool_quant_q(qp, Lq)
+    kbar, vbar, k8, ks, v16, _ = K.pool_quant_kv(k_full, v_full, Lk, ws=ws)
+    attn_full, attn_cond = K.predict(qbar, kbar, Lk.n_cand, full=order.kind == "restore_swap", cond=True)
+    nts, r = LY.select_blocks(attn_full, attn_cond, vbar, B, H, Lq.nq, Lk.n_cand, Lk.sink_blocks, budget, order,
+                              lead_blocks=lead_blocks, ws=ws)
+    o = K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"]).view(B, H, qp.shape[2], 64)
+    F_, S_, HW = geom.frames_local, geom.special, geom.hw
+    out = torch.empty(B, H, F_ * (S_ + HW), 64, dtype=torch.float32, device=dev)
+    view = out.view(B, H, F_, S_ + HW, 64)
+    view[:, :, :, S_:] = o[:, :, geom.lo: geom.lo + F_ * HW].view(B, H, F_, HW, 64)
+    main.wait_stream(side)
+    if x_special is not None:
+        x_special.record_stream(main)
+        view[:, :, :, :S_] = x_special.view(B, H, F_, S_, 64).float()
+    return ViewLayerResult(out=out, lists=r["lists"], counts=r["counts"], nts=nts, geom=geom)

@@ -135,3 +135,42 @@ def test_cuda_graph_replay_equals_eager():
         torch.cuda.synchronize()
         assert torch.equal(r.out, eager.out)
         assert torch.equal(r.counts, eager.counts)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_view_sharded_layer_equals_full(world):
+    """Frames sharded over `world` ranks, emulated in one process (the
+    all-gather hands every rank the other ranks' contributions): each rank's
+    budgets, keep lists and output rows are the unsharded layer's bits."""
+    from ress_b200 import shard
+
+    shape = synth.LayerShape(n_frames=8)
+    dev = torch.device("cuda", 0)
+    q, k, v = (t.to(dev) for t in synth.layer_qkv(shape, seed=2, dtype=torch.bfloat16, device=dev))
+    L = K.Layout(1, 16, shape.n_frames, shape.n_special, shape.hw)
+    M = synth.metric_from_weight(synth.out_proj_weight()).to(dev)
+    hs = synth.fisher_table(seed=1)[0, 4]
+    budget = LY.BudgetSpec("hess", sparse_ratio=0.5, scores_norm=K.scores_norm(hs).to(dev))
+    order = LY.OrderSpec("restore_swap", M=M)
+    ref = LY.global_layer(q, k, v, L, budget, order)
+    per = shape.n_frames // world * (shape.n_special + shape.hw)
+    geoms = [shard.ViewGeom(shape.n_frames, shape.n_special, shape.hw, world, r) for r in range(world)]
+    local = [tuple(t[:, :, r * per:(r + 1) * per].contiguous() for t in (q, k, v)) for r in range(world)]
+    parts = [shard.view_exchange_parts(*local[r], geoms[r]) for r in range(world)]
+
+    def gather(name, t):
+        return [p[name] for p in parts]
+
+    nq = L.nq
+    for r in range(world):
+        g = geoms[r]
+        res = shard.view_sharded_layer(*local[r], g, budget, order, gather)
+        torch.cuda.synchronize()
+        K.check_status(dev)
+        assert torch.equal(res.out, ref.out[:, :, r * per:(r + 1) * per])
+        ref_rows = torch.arange(16, device=dev)[:, None] * nq + torch.arange(g.b0, g.b1, device=dev)[None, :]
+        ref_rows = ref_rows.reshape(-1)
+        assert torch.equal(res.nts.view(16, -1), ref.nts.view(16, nq)[:, g.b0:g.b1])
+        assert torch.equal(res.counts, ref.counts[ref_rows])
+        valid = torch.arange(res.lists.shape[1], device=dev)[None, :] < res.counts[:, None]
+        assert torch.equal(torch.where(valid, res.lists, -1), torch.where(valid, ref.lists[ref_rows], -1))

@@ -51,3 +51,64 @@ def test_two_rank_hess_exchange():
     for r in range(2):
         assert torch.equal(res[r][0], _base())
         assert torch.equal(res[r][1], ref[:, 8 * r:8 * r + 8])
+
+
+# ----------------------------------------------------------------- views
+_VIEW = dict(frames=6, special=5, hw=100)  # 600 patch tokens: q-blocks straddle every shard boundary
+
+
+def _view_tensors():
+    g = torch.Generator().manual_seed(9)
+    T = _VIEW["frames"] * (_VIEW["special"] + _VIEW["hw"])
+    return [torch.randn(1, 4, T, 64, generator=g) for _ in range(3)]
+
+
+def _view_worker(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        geom = shard.ViewGeom(world=world, rank=rank, **_VIEW)
+        q, k, v = _view_tensors()
+        per = geom.frames_local * (geom.special + geom.hw)
+        sl = slice(rank * per, (rank + 1) * per)
+        qp, kf, vf = shard.view_assemble(q[:, :, sl].contiguous(), k[:, :, sl].contiguous(),
+                                         v[:, :, sl].contiguous(), geom, shard.make_view_gather(world))
+        out_q.put((rank, qp.numpy().copy(), kf.numpy().copy(), vf.numpy().copy()))  # by value
+    finally:
+        dist.destroy_process_group()
+
+
+def test_view_exchange_two_and_three_ranks():
+    """Each rank ends with every key and value, and with exactly the patch
+    queries of the global q-blocks that hold its tokens (halo from the
+    neighbours included)."""
+    ctx = mp.get_context("spawn")
+    q, k, v = _view_tensors()
+    qpatch = shard.patch_tokens(q, _VIEW["special"], _VIEW["hw"])
+    for world in (2, 3):
+        oq = ctx.Queue()
+        port = 30500 + os.getpid() % 1000 + world
+        procs = [ctx.Process(target=_view_worker, args=(r, world, port, oq)) for r in range(world)]
+        for p in procs:
+            p.start()
+        res = {r: tuple(torch.from_numpy(x) for x in (a, b, c)) for r, a, b, c in (oq.get(timeout=120) for _ in procs)}
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+        for r in range(world):
+            geom = shard.ViewGeom(world=world, rank=r, **_VIEW)
+            qp, kf, vf = res[r]
+            assert torch.equal(kf, k) and torch.equal(vf, v)
+            assert torch.equal(qp, qpatch[:, :, geom.b0 * 128: min(geom.b1 * 128, geom.Tp)])
+            assert (geom.lo > 0) == (r > 0) or geom.p0 % 128 == 0
+
+
+def test_view_geometry_config4():
+    """200 views over 8 ranks: q-block ranges tile the global grid with one
+    shared (straddling) block between neighbours."""
+    gs = [shard.ViewGeom(frames=200, special=5, hw=1369, world=8, rank=r) for r in range(8)]
+    assert gs[0].b0 == 0 and gs[-1].b1 == -(-200 * 1369 // 128)
+    for a, b in zip(gs, gs[1:]):
+        assert a.p1 == b.p0
+        assert b.b0 == a.b1 - 1 if a.p1 % 128 else b.b0 == a.b1
+        assert a.hi + b.lo == (128 if a.p1 % 128 else 0)
