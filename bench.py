@@ -52,6 +52,9 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-attn", action="store_true", help="one small layer, for ncu")
     ap.add_argument("--eager", action="store_true", help="time eager calls instead of CUDA-graph replays")
+    ap.add_argument("--shard", default="heads", choices=["heads", "views"],
+                    help="views: frames split over the ranks, K/V all-gathered (whole-model sharding)")
+    ap.add_argument("--sparse-ratio", type=float, default=None)
     return ap.parse_args()
 
 
@@ -456,6 +459,71 @@ def run_ress(args):
         torch.distributed.destroy_process_group()
 
 
+def run_views(args):
+    """One global layer with the frames split over the ranks (the whole-model
+    sharding of many-view runs): each rank owns frames/N frames, all-gathers
+    K and V with NCCL and runs its q-blocks.  Weak in queries, fixed layer."""
+    from ress_b200 import kernels as K
+    from ress_b200 import shard as SH
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    S = _setup(args.frames, 1, 0, device)
+    L = S["L"]
+    geom = SH.ViewGeom(args.frames, L.special, L.hw, ws, rank)
+    per = geom.frames_local * (L.special + L.hw)
+    q, k, v = (t[:, :, rank * per:(rank + 1) * per].contiguous() for t in (S["q"], S["k"], S["v"]))
+    del S["q"], S["k"], S["v"]
+    if ws > 1:
+        gather = SH.make_view_gather(ws)
+    else:
+        def gather(name, t):
+            return [t]
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        return SH.view_sharded_layer(q, k, v, geom, S["budget"], S["order"], gather)
+
+    for _ in range(max(3, args.warmup)):
+        res = step()
+    torch.cuda.synchronize()
+    K.check_status(device)
+    if ws > 1:
+        torch.distributed.barrier()
+    ms = _time_region(step, args.steps, stream)
+    torch.cuda.synchronize()
+    K.check_status(device)
+    t = torch.tensor([ms], device=device)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    kept = res.counts.sum().to(torch.float64)
+    rows = torch.tensor([float(res.counts.numel())], dtype=torch.float64, device=device)
+    if ws > 1:
+        torch.distributed.all_reduce(kept)
+        torch.distributed.all_reduce(rows)
+    width = L.n_cand + L.sink_blocks
+    if rank == 0:
+        line = {"metric": "global-attn layer throughput, view-sharded", "value": args.frames * args.steps / (ms / 1e3),
+                "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": max(3, args.warmup),
+                "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"one VGGT global layer, {args.frames} views, frames split over {ws} GPU(s), "
+                                       f"apply_ress(sparse_ratio={SPARSE_RATIO}), NCCL all-gather of K and V",
+                           "parallelism": f"views over {ws}", "sparsity": round(1 - float(kept.item()) /
+                                                                                 (float(rows.item()) * width), 4)}}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def profile_attn():
     """Small case for ncu: a 24-frame layer (int8 Q/K + fp16 V = 135 MB,
     above the 126 MB L2; under 1 GB on the device), two layers."""
@@ -469,8 +537,14 @@ def profile_attn():
 
 def main():
     args = _args()
+    global SPARSE_RATIO
+    if args.sparse_ratio is not None:
+        SPARSE_RATIO = args.sparse_ratio
     if args.profile_attn:
         profile_attn()
+        return
+    if args.shard == "views" and args.impl == "ress":
+        run_views(args)
         return
     if args.impl == "reference":
         run_reference(args)
