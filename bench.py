@@ -55,6 +55,8 @@ def _args():
     ap.add_argument("--shard", default="heads", choices=["heads", "views"],
                     help="views: frames split over the ranks, K/V all-gathered (whole-model sharding)")
     ap.add_argument("--sparse-ratio", type=float, default=None)
+    ap.add_argument("--sweep", action="store_true",
+                    help="standalone block-sparse attention: token counts x densities with random per-head maps")
     return ap.parse_args()
 
 
@@ -524,6 +526,51 @@ def run_views(args):
         torch.distributed.destroy_process_group()
 
 
+def run_sweep(args):
+    """The block-sparse attention op alone (config 5): Tp queries = Tk keys in
+    8K..300K, random per-(head, q-block) keep maps at densities 0.1..0.9,
+    16 heads x 64, bf16 inputs quantised like the layer.  One JSON line per
+    point; kernel time by CUDA events over `--steps` launches."""
+    from ress_b200 import kernels as K
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    bf16_peak, _, peak_src = _peaks()
+    mixed = 2.0 / (1.0 / bf16_peak + 1.0 / (2.0 * bf16_peak))
+    g = torch.Generator(device=device).manual_seed(0)
+    for T in (8192, 32768, 131072, 300032):
+        q, k, v = (torch.randn(1, 16, T, 64, device=device, generator=g, dtype=torch.float32).to(torch.bfloat16)
+                   for _ in range(3))
+        L = K.Layout.plain(q)
+        _, q8, qs = K.pool_quant_q(q, L, pool=False)
+        _, _, k8, ks, v16, _ = K.pool_quant_kv(k, v, L, pool=False)
+        del q, k, v
+        nq, nkb = L.nq, L.nkb
+        for dens in (0.1, 0.5, 0.9):
+            m = torch.rand(16 * nq, nkb, device=device, generator=g) < dens
+            lists, counts = K.map_to_lists(m)
+            out = torch.empty(16, T, 64, dtype=torch.float32, device=device)
+
+            def call():
+                K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out)
+
+            for _ in range(3):
+                call()
+            steps = max(3, min(args.steps, 20))
+            ms = _time_region(call, steps, stream) / steps
+            K.check_status(device)
+            flops = 4.0 * 128 * 64 * 64 * float(counts.sum().item())
+            tf = flops / (ms / 1e3) / 1e12
+            print(json.dumps({"metric": "block-sparse attention op (config 5)", "Tp": T, "density": dens,
+                              "kept_blocks": int(counts.sum().item()), "ms": round(ms, 4),
+                              "tflops": round(tf, 1), "frac": round(tf / mixed, 4),
+                              "peak_note": f"{peak_src} mixed int8/bf16 peak {mixed:.0f} TF/s"}), flush=True)
+            del lists, counts, m, out
+        del q8, qs, k8, ks, v16
+        torch.cuda.empty_cache()
+
+
 def profile_attn():
     """Small case for ncu: a 24-frame layer (int8 Q/K + fp16 V = 135 MB,
     above the 126 MB L2; under 1 GB on the device), two layers."""
@@ -542,6 +589,9 @@ def main():
         SPARSE_RATIO = args.sparse_ratio
     if args.profile_attn:
         profile_attn()
+        return
+    if args.sweep:
+        run_sweep(args)
         return
     if args.shard == "views" and args.impl == "ress":
         run_views(args)

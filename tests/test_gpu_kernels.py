@@ -228,3 +228,32 @@ def test_sparse_attention_full_layout_and_leading_sink():
     assert torch.isnan(special).all()  # special rows are left for the dense branch
     lists = sel["lists"].cpu()
     assert (lists[:, 0] == 0).all()  # leading sink block forced in
+
+
+@pytest.mark.parametrize("density", [0.1, 0.9])
+def test_sparse_attention_random_maps(density):
+    """Arbitrary keep lists (uniformly random per row, no structure) on a
+    plain (patch-only) layout with a ragged key tail: sampled rows within
+    2e-2 max / 1e-3 mean abs of the fp64 oracle."""
+    g = torch.Generator().manual_seed(int(density * 10))
+    T = 3000  # 24 q-blocks, 47 key blocks, last one ragged
+    q, k, v = (torch.randn(1, 4, T, 64, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
+    L = K.Layout.plain(q)
+    _, q8, qs = K.pool_quant_q(q, L, pool=False)
+    _, _, k8, ks, v16, _ = K.pool_quant_kv(k, v, L, pool=False)
+    m = torch.rand(4 * L.nq, L.nkb, generator=g) < density
+    m[:, 0] = True  # every row keeps at least one block
+    lists, counts = K.map_to_lists(m.cuda())
+    out = K.sparse_attn(q8, qs, k8, ks, v16, lists, counts)
+    torch.cuda.synchronize()
+    K.check_status()
+    samples = [(h, b) for h in range(4) for b in (0, 7, L.nq - 1)]
+    ref = oracle.sparse_attn_rows(q8.cpu(), qs.cpu(), k8.cpu(), ks.cpu(), v16.cpu().float(),
+                                  lists.view(4, L.nq, -1).cpu(), counts.view(4, L.nq).cpu(), samples)
+    errs = []
+    for i, (h, b) in enumerate(samples):
+        n = min(128, T - b * 128)
+        errs.append((out[h, b * 128: b * 128 + n].cpu() - ref[i, :n]).abs().reshape(-1))
+    e = torch.cat(errs)
+    assert e.max().item() < 2e-2, e.max().item()
+    assert e.mean().item() < 1e-3, e.mean().item()
