@@ -55,6 +55,8 @@ def _args():
     ap.add_argument("--shard", default="heads", choices=["heads", "views"],
                     help="views: frames split over the ranks, K/V all-gathered (whole-model sharding)")
     ap.add_argument("--sparse-ratio", type=float, default=None)
+    ap.add_argument("--model", default=None, choices=["vggt"],
+                    help="whole VGGT-1B-shaped aggregator (configs 3/4) instead of one global layer")
     ap.add_argument("--sweep", action="store_true",
                     help="standalone block-sparse attention: token counts x densities with random per-head maps")
     return ap.parse_args()
@@ -571,6 +573,96 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+def run_model(args):
+    """The whole VGGT-1B-shaped aggregator (random init, bf16): patch encoder,
+    24 frame + 24 global blocks, intermediates at 4/11/17/23, on uniform
+    [0, 1) images of 518 x 518.  Global attention through the package's
+    apply_ress (HeSS budget from synthetic log-normal tables, lambda 0.5,
+    restore-swap 5 rounds).  Under torchrun the views are sharded: frame
+    blocks stay local and each global block all-gathers K/V with NCCL."""
+    import tempfile
+
+    from ress_b200 import api, shard as SH, synth, vggt, wiring
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    N = args.frames
+    if N % ws:
+        raise SystemExit(f"{N} views do not split over {ws} GPUs")
+    nl = N // ws
+    torch.manual_seed(0)
+    model = vggt.VGGTAggregatorModel().to(device=device, dtype=torch.bfloat16).eval()
+    g = torch.Generator(device=device).manual_seed(1)
+    images = torch.rand(1, N, 3, 518, 518, device=device, generator=g)[:, rank * nl:(rank + 1) * nl].contiguous()
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+
+    dense_ms = None
+    if ws == 1:
+        with torch.inference_mode():
+            def dense_step():
+                model(images)
+            for _ in range(2):
+                dense_step()
+            torch.cuda.synchronize()
+            dense_ms = _time_region(dense_step, max(2, min(args.steps, 5)), stream) / max(2, min(args.steps, 5))
+
+    tables = tempfile.mkdtemp(prefix="ress_tables_")
+    torch.save(synth.fisher_table(24, 16, seed=1), os.path.join(tables, "fisher_scores_vggt_cam_pos.pt"))
+    torch.save(synth.fisher_table(24, 16, seed=3), os.path.join(tables, "fisher_scores_vggt_pcd.pt"))
+    os.environ["RESS_CALIBRATION_DIR"] = tables
+    wiring.wire_ress_attention(model, model.aggregator.global_blocks, num_special_tokens=5)
+    model._ress_backbone = "vggt"
+    api.apply_ress(model, sparse_ratio=SPARSE_RATIO, n_iters=5)
+    for blk in model.aggregator.global_blocks:
+        blk.attn.ress_shape = {"H": 37, "W": 37, "N": nl}  # token split without a host read of pos
+    if ws > 1:
+        geom = SH.ViewGeom(N, 5, 1369, ws, rank)
+        gather = SH.make_view_gather(ws)
+        for blk in model.aggregator.global_blocks:
+            blk.attn.ress_view = (geom, gather)
+
+    with torch.inference_mode():
+        def step():
+            model(images, first_frame=(rank == 0))
+        for _ in range(max(2, min(args.warmup, 3))):
+            step()
+        torch.cuda.synchronize()
+        barrier()
+        steps = max(2, min(args.steps, 10))
+        with Clocks(local) as clk:
+            ms = _time_region(step, steps, stream)
+        torch.cuda.synchronize()
+    t = torch.tensor([ms], device=device)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item()) / steps
+    if rank == 0:
+        line = {"metric": "VGGT aggregator views/s", "value": N / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
+                "steps": steps, "warmup": max(2, min(args.warmup, 3)), "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (uniform [0,1) images, random-init weights)",
+                "config": {"workload": f"VGGT-1B-shaped aggregator, {N} views of 518x518, apply_ress("
+                                       f"sparse_ratio={SPARSE_RATIO}, n_iters=5), HeSS lambda 0.5",
+                           "parallelism": f"views over {ws} GPU(s)" + (", NCCL all-gather of K/V per global block"
+                                                                        if ws > 1 else "")},
+                "torch_dense_ms_per_step": dense_ms,
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def profile_attn():
     """Small case for ncu: a 24-frame layer (int8 Q/K + fp16 V = 135 MB,
     above the 126 MB L2; under 1 GB on the device), two layers."""
@@ -592,6 +684,9 @@ def main():
         return
     if args.sweep:
         run_sweep(args)
+        return
+    if args.model == "vggt" and args.impl == "ress":
+        run_model(args)
         return
     if args.shard == "views" and args.impl == "ress":
         run_views(args)

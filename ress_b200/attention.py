@@ -195,10 +195,24 @@ def ress_attention_forward(self, x, pos, num_to_select=None, budget_fn=None, per
             def pbf(attn_cond, _f=perhead_budget_fn):
                 vb = block_mean_value(get_patch_tokens(v, N, P, S))[..., : L.n_cand, :]
                 return _f(attn_cond, vb)
-        res = global_layer(q, k, v, L, budget, order, num_to_select=num_to_select,
-                           budget_fn=pbf or budget_fn, keep_pooled=aux_store is not None,
-                           joint_select_fn=joint_select_fn, map_hook=hook)
-        x_out = res.out
+        view = getattr(self, "ress_view", None)
+        if view is not None:
+            # frames of this rank only; K/V are all-gathered inside (whole-model view sharding)
+            if budget is None or joint_select_fn is not None or hook is not None or pbf is not None:
+                raise NotImplementedError("view sharding runs the package's own budgets and orders")
+            from .shard import view_sharded_layer
+
+            geom, gather = view
+            res = view_sharded_layer(q, k, v, geom, budget, order, gather)
+            x_out = res.out
+            sparsity = 0.0 if aux_store is None else None
+            if aux_store is not None:
+                raise NotImplementedError("aux outputs are not collected under view sharding")
+        else:
+            res = global_layer(q, k, v, L, budget, order, num_to_select=num_to_select,
+                               budget_fn=pbf or budget_fn, keep_pooled=aux_store is not None,
+                               joint_select_fn=joint_select_fn, map_hook=hook)
+            x_out = res.out
         sparsity = None
     if aux_store is not None:
         if sparsity is None:

@@ -62,4 +62,9 @@ def combine_special_and_patch(x_special, x_patch, shape):
 
 def project_out(self, x, B, N, P, nh, hd):
     x = x.transpose(1, 2).reshape(B, N * P, nh * hd)
+    w = self.proj.weight
+    if x.dtype != w.dtype and not torch.is_autocast_enabled():
+        # the sparse kernel writes fp32 (attention.py:243); a model held in
+        # bf16 without autocast projects in its own dtype
+        x = x.to(w.dtype)
     return self.proj_drop(self.proj(x))
