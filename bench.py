@@ -141,10 +141,6 @@ def _setup(frames, world, rank, device):
     if H % world:
         raise SystemExit(f"{H} heads do not split over {world} GPUs")
     hl = H // world
-    h0 = rank * hl
-    q, k, v = (t[:, h0:h0 + hl].contiguous() for t in (q, k, v))
-    L = K.Layout(1, hl, shape.n_frames, shape.n_special, shape.hw)
-    M = synth.metric_from_weight(synth.out_proj_weight(), H)[h0:h0 + hl].to(device)
     # HessBudget tables: row 0 (W_Q) of two log-normal (3, 24, 16) tables, lambda = 0.5, layer 0
     cam, pcd = synth.fisher_table(seed=1)[0], synth.fisher_table(seed=3)[0]
     cam = cam / cam.sum(-1, keepdim=True)
@@ -153,16 +149,24 @@ def _setup(frames, world, rank, device):
     head_scores = (comb / comb.sum(-1, keepdim=True))[0]
     sn = K.scores_norm(head_scores).to(device)
     shard = None
+    heads = list(range(H))
     if world > 1:
         from ress_b200 import shard as SH
 
-        shard = SH.make_head_shard(H, world, rank)
+        # heads balanced over the GPUs by their HeSS scores (budgets grow with the score)
+        shard = SH.make_head_shard(H, world, rank, scores=head_scores, cap=1.0 / (1.0 - SPARSE_RATIO))
+        heads = list(shard.heads)
+    hidx = torch.as_tensor(heads, dtype=torch.long, device=device)
+    q, k, v = (t.index_select(1, hidx).contiguous() for t in (q, k, v))
+    L = K.Layout(1, hl, shape.n_frames, shape.n_special, shape.hw)
+    M = synth.metric_from_weight(synth.out_proj_weight(), H)[hidx.cpu()].to(device)
+    h0 = heads[0]
     budget = LY.BudgetSpec("hess", sparse_ratio=SPARSE_RATIO, cdf_threshold=None, scores_norm=sn)
     budget_hess = LY.BudgetSpec("hess", sparse_ratio=SPARSE_RATIO, cdf_threshold=CDF, scores_norm=sn)
     order = LY.OrderSpec("restore_swap", M=M, n_iters=5, track_best=True)
     order_prob = LY.OrderSpec("probability")
     return dict(shape=shape, q=q, k=k, v=v, L=L, budget=budget, budget_hess=budget_hess, order=order,
-                order_prob=order_prob, shard=shard, h0=h0, hl=hl)
+                order_prob=order_prob, shard=shard, h0=h0, hl=hl, heads=heads)
 
 
 def _attn_flops(lists, counts, L):
@@ -341,7 +345,7 @@ def run_ress(args):
             base = S["shard"].gather(base)
         nts = K.hess_adjust(base, S["budget"].scores_norm, L.n_cand, min_clamp=2)
         if S["shard"] is not None:
-            nts = nts[:, S["h0"]:S["h0"] + L.H].contiguous()
+            nts = S["shard"].select(nts, L.H)
         ev[2].record(stream)
         r = K.restore_swap(af, vbar, S["order"].M, nts.view(-1), L.n_cand, sink_blocks=L.sink_blocks)
         ev[3].record(stream)

@@ -72,6 +72,12 @@ class HeadShard:
     h0: int
     h_total: int
     gather: object
+    heads: tuple | None = None  # this rank's global head indices when not the contiguous [h0, h0 + H_local)
+
+    def select(self, full: torch.Tensor, H: int) -> torch.Tensor:
+        if self.heads is None:
+            return full[:, self.h0: self.h0 + H].contiguous()
+        return full.index_select(1, torch.as_tensor(self.heads, dtype=torch.long, device=full.device))
 
 
 @dataclass
@@ -149,7 +155,7 @@ def select_blocks(attn_full, attn_cond, vbar, B: int, H: int, nq: int, n_cand: i
         if budget.kind == "hess" and shard is not None:
             full = shard.gather(base)
             nts_full = K.hess_adjust(full, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
-            nts = nts_full[:, shard.h0: shard.h0 + H].contiguous()
+            nts = shard.select(nts_full, H)
         elif budget.kind == "hess":
             nts = K.hess_adjust(base, budget.scores_norm, n_cand, beta=budget.beta, min_clamp=min_sel)
         else:

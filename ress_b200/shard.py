@@ -26,18 +26,85 @@ def head_range(n_heads: int, world: int, rank: int):
     return rank * hl, hl
 
 
-def make_gather(world: int, group=None):
-    """base (B, H_local, nq) int32 -> (B, world * H_local, nq), rank order."""
+def budget_shares(scores, cap: float | None = None) -> list:
+    """Each head's expected share of the layer's blocks under HeSS, in units
+    of the mean head budget: proportional to its score, capped at `cap` (all
+    candidate blocks, i.e. n_cand / baseline = 1 / (1 - sparse_ratio)) with
+    the excess spread over the uncapped heads in proportion, the way
+    ``adjust_attention_selection`` re-allocates (budget/_proportional.py)."""
+    s = [max(float(x), 0.0) for x in scores]
+    H = len(s)
+    tot = sum(s) or 1.0
+    w = [x / tot * H for x in s]
+    if cap is None:
+        return w
+    capped = [False] * H
+    for _ in range(H):
+        over = [i for i in range(H) if not capped[i] and w[i] > cap]
+        if not over:
+            break
+        for i in over:
+            capped[i] = True
+        excess = sum(w[i] - cap for i in over)
+        for i in over:
+            w[i] = cap
+        free = sum(w[i] for i in range(H) if not capped[i])
+        if free <= 0:
+            break
+        for i in range(H):
+            if not capped[i]:
+                w[i] += excess * w[i] / free
+    return w
+
+
+def balanced_heads(scores, world: int, cap: float | None = None) -> list:
+    """Partition the heads into `world` equal-size groups whose summed
+    expected budgets (``budget_shares``) are as even as a greedy pass makes
+    them (heaviest head first, to the lightest group with room).  The result
+    depends only on the scores, so every rank computes the same one."""
+    s = budget_shares(scores, cap)
+    H = len(s)
+    if H % world:
+        raise ValueError(f"{H} heads do not split evenly over {world} ranks")
+    per = H // world
+    groups = [[] for _ in range(world)]
+    sums = [0.0] * world
+    for h in sorted(range(H), key=lambda i: (-s[i], i)):
+        g = min((i for i in range(world) if len(groups[i]) < per), key=lambda i: (sums[i], i))
+        groups[g].append(h)
+        sums[g] += s[h]
+    return [sorted(g) for g in groups]
+
+
+def make_gather(world: int, group=None, order=None):
+    """base (B, H_local, nq) int32 -> (B, world * H_local, nq): rank order, or
+    global head order when `order` (the heads of every rank, rank after rank)
+    is given."""
+    inv = None
+    if order is not None:
+        inv = torch.empty(len(order), dtype=torch.long)
+        inv[torch.as_tensor(order, dtype=torch.long)] = torch.arange(len(order))
+
     def gather(base: torch.Tensor) -> torch.Tensor:
         parts = [torch.empty_like(base) for _ in range(world)]
         dist.all_gather(parts, base.contiguous(), group=group)
-        return torch.cat(parts, dim=1)
+        full = torch.cat(parts, dim=1)
+        if inv is not None:
+            full = full.index_select(1, inv.to(full.device))
+        return full
     return gather
 
 
-def make_head_shard(n_heads: int, world: int, rank: int, group=None) -> HeadShard:
-    h0, _ = head_range(n_heads, world, rank)
-    return HeadShard(h0=h0, h_total=n_heads, gather=make_gather(world, group))
+def make_head_shard(n_heads: int, world: int, rank: int, group=None, scores=None, cap=None) -> HeadShard:
+    """Contiguous head ranges, or with `scores` (the layer's HeSS head scores)
+    the balanced partition of ``balanced_heads``."""
+    if scores is None:
+        h0, _ = head_range(n_heads, world, rank)
+        return HeadShard(h0=h0, h_total=n_heads, gather=make_gather(world, group))
+    parts = balanced_heads(scores, world, cap)
+    order = [h for p in parts for h in p]
+    return HeadShard(h0=parts[rank][0], h_total=n_heads, gather=make_gather(world, group, order),
+                     heads=tuple(parts[rank]))
 
 
 # ----------------------------------------------------------------- views

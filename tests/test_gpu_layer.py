@@ -116,6 +116,51 @@ def test_head_split_equals_full():
         assert (ps - fs).abs().max().item() < 1e-2
 
 
+def test_balanced_head_split_equals_full():
+    """Heads split by the balanced partition (non-contiguous head sets per
+    rank), baselines gathered back into global head order: each rank's
+    lists and patch outputs are the unsplit layer's."""
+    from ress_b200 import shard as SH
+
+    shape, dtype = synth.LayerShape(n_frames=6), torch.bfloat16
+    q, k, v = _data(shape, dtype)
+    dev = torch.device("cuda", 0)
+    M = synth.metric_from_weight(synth.out_proj_weight()).to(dev)
+    hs = synth.fisher_table(seed=1)[0, 5]
+    sn = K.scores_norm(hs)
+    budget = LY.BudgetSpec("hess", sparse_ratio=0.5, scores_norm=sn)
+    L = K.Layout(1, 16, shape.n_frames, shape.n_special, shape.hw)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    full = LY.global_layer(qd, kd, vd, L, budget, LY.OrderSpec("restore_swap", M=M))
+    world = 4
+    parts = SH.balanced_heads(hs, world, cap=2.0)
+    assert sorted(h for p in parts for h in p) == list(range(16))
+    assert any(p != list(range(p[0], p[0] + 4)) for p in parts)  # not all contiguous
+    Lg = K.Layout(1, 4, shape.n_frames, shape.n_special, shape.hw)
+    base_all = torch.empty(1, 16, L.nq, dtype=torch.int32, device=dev)
+    for p in parts:
+        hidx = torch.as_tensor(p, device=dev)
+        qbar, _, _ = K.pool_quant_q(qd.index_select(1, hidx).contiguous(), Lg, quant=False)
+        kbar, _, _, _, _, _ = K.pool_quant_kv(kd.index_select(1, hidx).contiguous(),
+                                              vd.index_select(1, hidx).contiguous(), Lg, quant=False)
+        _, ac = K.predict(qbar, kbar, Lg.n_cand, full=False)
+        base_all[:, hidx] = K.baseline(ac, 0.5).view(1, 4, -1)
+    w = L.n_cand + L.sink_blocks
+    for p in parts:
+        hidx = torch.as_tensor(p, device=dev)
+        sh = LY.HeadShard(h0=p[0], h_total=16, gather=lambda base, _g=base_all: _g, heads=tuple(p))
+        part = LY.global_layer(qd.index_select(1, hidx).contiguous(), kd.index_select(1, hidx).contiguous(),
+                               vd.index_select(1, hidx).contiguous(), Lg, budget,
+                               LY.OrderSpec("restore_swap", M=M[hidx]), shard=sh)
+        rows = (hidx[:, None] * L.nq + torch.arange(L.nq, device=dev)[None, :]).reshape(-1)
+        assert torch.equal(part.counts, full.counts[rows])
+        assert torch.equal(K.lists_to_map(part.lists, part.counts, w),
+                           K.lists_to_map(full.lists[rows], full.counts[rows], w))
+        pp, _ = synth.split_tokens(part.out.cpu(), shape)
+        fp, _ = synth.split_tokens(full.out[:, hidx].cpu(), shape)
+        assert torch.equal(pp, fp)
+
+
 def test_cuda_graph_replay_equals_eager():
     """The layer captured in a CUDA graph (library kernels, side-stream SDPA)
     replays to the same bits as the eager call."""

@@ -112,3 +112,46 @@ def test_view_geometry_config4():
         assert a.p1 == b.p0
         assert b.b0 == a.b1 - 1 if a.p1 % 128 else b.b0 == a.b1
         assert a.hi + b.lo == (128 if a.p1 % 128 else 0)
+
+
+def _bal_worker(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        sh = shard.make_head_shard(16, world, rank, scores=_scores(), cap=2.0)
+        local = _base().index_select(1, torch.as_tensor(sh.heads)).contiguous()
+        full = sh.gather(local)
+        nts = oracle.hess_adjust(full, oracle.scores_norm(_scores()), 60, min_clamp=2)
+        out_q.put((rank, full.numpy().copy(), sh.select(nts, len(sh.heads)).numpy().copy(), list(sh.heads)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_balanced_head_exchange_four_ranks():
+    """Balanced (non-contiguous) head sets: the gathered baselines come back in
+    global head order and each rank keeps its own heads' budgets."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 31500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_bal_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = {r: (f, n, h) for r, f, n, h in (q.get(timeout=120) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = oracle.hess_adjust(_base(), oracle.scores_norm(_scores()), 60, min_clamp=2)
+    seen = []
+    for r in range(4):
+        full, nts, heads = res[r]
+        assert torch.equal(torch.from_numpy(full), _base())
+        assert torch.equal(torch.from_numpy(nts), ref[:, heads])
+        seen += heads
+    assert sorted(seen) == list(range(16))
+
+
+def test_budget_shares_cap():
+    s = torch.tensor([10.0] + [1.0] * 7)
+    w = shard.budget_shares(s, cap=2.0)
+    assert abs(sum(w) - 8.0) < 1e-9 and abs(w[0] - 2.0) < 1e-9
+    assert all(abs(x - 6.0 / 7.0) < 1e-9 for x in w[1:])
