@@ -77,7 +77,12 @@ class HeadShard:
     def select(self, full: torch.Tensor, H: int) -> torch.Tensor:
         if self.heads is None:
             return full[:, self.h0: self.h0 + H].contiguous()
-        return full.index_select(1, torch.as_tensor(self.heads, dtype=torch.long, device=full.device))
+        # the index lives on the device from the first (eager) call on: no host copy during graph capture
+        cache = self.__dict__.setdefault("_idx", {})
+        idx = cache.get(full.device)
+        if idx is None:
+            idx = cache[full.device] = torch.as_tensor(self.heads, dtype=torch.long, device=full.device)
+        return full.index_select(1, idx)
 
 
 @dataclass

@@ -84,13 +84,17 @@ def make_gather(world: int, group=None, order=None):
     if order is not None:
         inv = torch.empty(len(order), dtype=torch.long)
         inv[torch.as_tensor(order, dtype=torch.long)] = torch.arange(len(order))
+    on_device = {}  # device copies, made on the first (eager) call: no host copy inside a graph capture
 
     def gather(base: torch.Tensor) -> torch.Tensor:
         parts = [torch.empty_like(base) for _ in range(world)]
         dist.all_gather(parts, base.contiguous(), group=group)
         full = torch.cat(parts, dim=1)
         if inv is not None:
-            full = full.index_select(1, inv.to(full.device))
+            idx = on_device.get(full.device)
+            if idx is None:
+                idx = on_device[full.device] = inv.to(full.device)
+            full = full.index_select(1, idx)
         return full
     return gather
 
