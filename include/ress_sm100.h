@@ -61,6 +61,12 @@ enum {
 enum { RESS_F32 = 0, RESS_BF16 = 1 };
 
 int ress_version(void);
+
+/* Self-check of the quantisers' division (no reference counterpart): counts
+ * into *mismatches (device int32, caller-zeroed) the (x, amax) fp16 pairs,
+ * |x| <= amax, whose quotient x / RN(amax/127) the quantisers' reciprocal-
+ * and-correction division rounds differently from IEEE division. */
+int ress_check_scale_division(int32_t *mismatches, ress_stream_t stream);
 const char *ress_error_string(int code);
 
 /*

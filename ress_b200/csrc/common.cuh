@@ -101,6 +101,19 @@ __device__ __forceinline__ float ress_expf(float x) {
     return __fmul_rn(p, __int_as_float((-100 + 127) << 23));
 }
 
+// x / d rounded to nearest, for a divisor d shared by many numerators:
+// Markstein's correction step (P. Markstein, IBM J. Res. Dev. 34(1), 1990):
+// with r = RN(1/d) and q = RN(x * r), the remainder x - q*d is exact in one
+// fma and RN(q + rem * r) is the correctly rounded quotient.  The
+// quantisers use it for x an fp16 value with |x| <= amax and d = RN(amax /
+// 127); ress_check_scale_division compares it with IEEE division over that
+// entire domain.
+__device__ __forceinline__ float div_by(float x, float d, float r) {
+    const float q = __fmul_rn(x, r);
+    const float rem = __fmaf_rn(-q, d, x);
+    return __fmaf_rn(rem, r, q);
+}
+
 // Order-preserving uint32 key (fused_topm.py:51-56): -0 < +0.
 __device__ __forceinline__ uint32_t order_key(float x) {
     uint32_t u = __float_as_uint(x);

@@ -47,6 +47,30 @@ __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16 *src, f
 
 constexpr int POOL_NT = 256;
 
+// Quantisation code of y = x / scale: trunc(RN(y + 0.5 * sign(y))).  With
+// w = RN(|y| + 0.5) (RN is symmetric, so this is |RN(y +- 0.5)|) the code is
+// sign(y) * floor(w); for 0 <= w < 2^23 the round-toward-zero sum w + 2^23
+// holds floor(w) in its low mantissa bits.  No conversion instruction.
+__device__ __forceinline__ int quant_code(float y) {
+    const float w = __fadd_rn(fabsf(y), 0.5f);
+    const int m = (int)(__float_as_uint(__fadd_rz(w, 8388608.0f)) - 0x4B000000u);
+    return (__float_as_uint(y) >> 31) ? -m : m;
+}
+
+// fp16 rounding of a value that came from T.  A bf16 value inside fp16's
+// normal range [2^-14, 65520) has at most 8 significant bits and is exactly
+// an fp16 value, so only values outside it take the conversion.
+template <typename T>
+__device__ __forceinline__ float f16r_from(float x) {
+    if constexpr (sizeof(T) == 2) {
+        const float a = fabsf(x);
+        if (a >= 6.103515625e-05f && a < 65520.0f) return x;
+        return a == 0.0f ? x : f16r(x);
+    } else {
+        return f16r(x);
+    }
+}
+
 // Quantise a tile of fp16-valued floats (rows x 64, row stride 65) held in
 // shared memory: scale = amax/127, q = trunc(x/scale + 0.5*sign(x)).
 __device__ __forceinline__ void quant_tile(const float (*tile)[65], int rows, int8_t *dst,
@@ -55,6 +79,7 @@ __device__ __forceinline__ void quant_tile(const float (*tile)[65], int rows, in
     for (int i = threadIdx.x; i < rows * 64; i += POOL_NT) amax = fmaxf(amax, fabsf(tile[i >> 6][i & 63]));
     amax = block_max_float<POOL_NT>(amax, red);
     float sc = __fdiv_rn(amax, 127.0f);
+    const float rc = sc != 0.0f ? __frcp_rn(sc) : 0.0f;
     if (threadIdx.x == 0) *scale_out = sc;
     // 8 consecutive codes per thread -> one 8-byte store
     for (int i = threadIdx.x; i < rows * 8; i += POOL_NT) {
@@ -62,13 +87,8 @@ __device__ __forceinline__ void quant_tile(const float (*tile)[65], int rows, in
         uint32_t w[2] = {0u, 0u};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            int8_t qv = 0;
-            if (sc != 0.0f) {
-                float v = __fdiv_rn(tile[r][c + j], sc);
-                v = __fadd_rn(v, v >= 0.0f ? 0.5f : -0.5f);
-                qv = (int8_t)truncf(v);
-            }
-            w[j >> 2] |= ((uint32_t)(uint8_t)qv) << ((j & 3) * 8);
+            const int qv = sc != 0.0f ? quant_code(div_by(tile[r][c + j], sc, rc)) : 0;
+            w[j >> 2] |= ((uint32_t)(uint8_t)(int8_t)qv) << ((j & 3) * 8);
         }
         *reinterpret_cast<uint2 *>(dst + (size_t)r * 64 + c) = make_uint2(w[0], w[1]);
     }
@@ -79,31 +99,104 @@ template <typename T>
 __global__ void __launch_bounds__(POOL_NT) pool_q_kernel(
     const T *__restrict__ q, int H, int S, int HW, int Tp, long long sb, long long sh,
     long long st, T *__restrict__ qbar, int8_t *__restrict__ q8, float *__restrict__ qscale) {
-    __shared__ float tile[KS_Q][65];
+    // one buffer: the fp32 tile, or (bf16 input) the raw bf16 tile
+    __shared__ __align__(16) float tile_raw[KS_Q * 65];
     __shared__ float red[32];
+    float(*tile)[65] = reinterpret_cast<float(*)[65]>(tile_raw);
     const int qb = blockIdx.x, bh = blockIdx.y, nqb = gridDim.x;
     const int b = bh / H, h = bh - b * H;
     const T *base = q + b * sb + h * sh;
     const int t0 = qb * KS_Q, cnt = min(KS_Q, Tp - t0);
-    for (int i = threadIdx.x; i < KS_Q * 8; i += POOL_NT) {
-        int r = i >> 3, c = (i & 7) * 8;
-        float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (r < cnt) load8<T>(base + patch_tok(t0 + r, S, HW) * st + c, v);
+    if constexpr (sizeof(T) == 2) {
+        // bf16: each thread keeps its 4 x 8 values in registers; the tile in
+        // shared memory only feeds the column sums of the pooled mean
+        uint16_t(*tb)[72] = reinterpret_cast<uint16_t(*)[72]>(tile_raw);
+        uint4 u[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) tile[r][c + j] = v[j];
+        for (int k = 0; k < 4; ++k) {
+            const int i = threadIdx.x + k * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+            u[k] = make_uint4(0u, 0u, 0u, 0u);
+            if (r < cnt) u[k] = *reinterpret_cast<const uint4 *>(base + patch_tok(t0 + r, S, HW) * st + c);
+            *reinterpret_cast<uint4 *>(&tb[r][c]) = u[k];
+        }
+        // |x| maximum on the bit patterns (non-negative floats order as integers)
+        unsigned mx2 = 0u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            mx2 = __vmaxu2(mx2, u[k].x & 0x7FFF7FFFu);
+            mx2 = __vmaxu2(mx2, u[k].y & 0x7FFF7FFFu);
+            mx2 = __vmaxu2(mx2, u[k].z & 0x7FFF7FFFu);
+            mx2 = __vmaxu2(mx2, u[k].w & 0x7FFF7FFFu);
+        }
+        const float amax_raw = block_max_float<POOL_NT>(
+            fmaxf(__uint_as_float(mx2 << 16), __uint_as_float(mx2 & 0xFFFF0000u)), red);  // syncs: tb complete
+        if (qbar != nullptr && threadIdx.x < HD) {
+            const int d = threadIdx.x;
+            float s = 0.0f;
+            for (int t = 0; t < cnt; ++t) s = __fadd_rn(s, __uint_as_float((uint32_t)tb[t][d] << 16));
+            DT<T>::store(qbar, ((size_t)bh * nqb + qb) * HD + d, __fdiv_rn(s, (float)cnt));
+        }
+        if (q8 == nullptr) return;
+        // fp16 rounding is monotone, so the tile maximum of fp16(x) is fp16(max |x|).  In
+        // [0.0157, 65520) every bf16 x of fp16's normal range is exactly an fp16 value, and
+        // every |x| < 2^-14 (which fp16 would round) quantises to 0 either way: |x / scale|
+        // stays below 0.5 - 2^-25, so x itself can be divided
+        if (amax_raw >= 0.0157f && amax_raw < 65520.0f) {
+            const float sc = __fdiv_rn(amax_raw, 127.0f);  // amax_raw is exact in fp16
+            const float rc = __frcp_rn(sc);
+            if (threadIdx.x == 0) qscale[(size_t)bh * nqb + qb] = sc;
+            int8_t *dst = q8 + ((size_t)bh * Tp + t0) * HD;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = threadIdx.x + k * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+                if (r >= cnt) continue;
+                const uint32_t wv[4] = {u[k].x, u[k].y, u[k].z, u[k].w};
+                uint32_t w[2] = {0u, 0u};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float x = __uint_as_float(j & 1 ? (wv[j >> 1] & 0xFFFF0000u) : (wv[j >> 1] << 16));
+                    const int qv = quant_code(div_by(x, sc, rc));
+                    w[j >> 2] |= ((uint32_t)(uint8_t)(int8_t)qv) << ((j & 3) * 8);
+                }
+                *reinterpret_cast<uint2 *>(dst + (size_t)r * 64 + c) = make_uint2(w[0], w[1]);
+            }
+            return;
+        }
+        // outside the window: fp16-round every value into the fp32 tile (the
+        // bf16 tile's storage, free once the column sums are done)
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = threadIdx.x + k * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+            const uint32_t wv[4] = {u[k].x, u[k].y, u[k].z, u[k].w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                tile[r][c + j] = f16r(__uint_as_float(j & 1 ? (wv[j >> 1] & 0xFFFF0000u) : (wv[j >> 1] << 16)));
+        }
+        __syncthreads();
+        quant_tile(tile, cnt, q8 + ((size_t)bh * Tp + t0) * HD, qscale + (size_t)bh * nqb + qb, red);
+        return;
+    } else {
+        for (int i = threadIdx.x; i < KS_Q * 8; i += POOL_NT) {
+            int r = i >> 3, c = (i & 7) * 8;
+            float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (r < cnt) load8<T>(base + patch_tok(t0 + r, S, HW) * st + c, v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tile[r][c + j] = v[j];
+        }
+        __syncthreads();
+        if (qbar != nullptr && threadIdx.x < HD) {
+            const int d = threadIdx.x;
+            float s = 0.0f;
+            for (int t = 0; t < cnt; ++t) s = __fadd_rn(s, tile[t][d]);
+            DT<T>::store(qbar, ((size_t)bh * nqb + qb) * HD + d, __fdiv_rn(s, (float)cnt));
+        }
+        if (q8 == nullptr) return;
+        __syncthreads();
+        for (int i = threadIdx.x; i < cnt * HD; i += POOL_NT) tile[i >> 6][i & 63] = f16r(tile[i >> 6][i & 63]);
+        __syncthreads();
+        quant_tile(tile, cnt, q8 + ((size_t)bh * Tp + t0) * HD, qscale + (size_t)bh * nqb + qb, red);
     }
-    __syncthreads();
-    if (qbar != nullptr && threadIdx.x < HD) {
-        const int d = threadIdx.x;
-        float s = 0.0f;
-        for (int t = 0; t < cnt; ++t) s = __fadd_rn(s, tile[t][d]);
-        DT<T>::store(qbar, ((size_t)bh * nqb + qb) * HD + d, __fdiv_rn(s, (float)cnt));
-    }
-    if (q8 == nullptr) return;
-    __syncthreads();
-    for (int i = threadIdx.x; i < cnt * HD; i += POOL_NT) tile[i >> 6][i & 63] = f16r(tile[i >> 6][i & 63]);
-    __syncthreads();
-    quant_tile(tile, cnt, q8 + ((size_t)bh * Tp + t0) * HD, qscale + (size_t)bh * nqb + qb, red);
 }
 
 // Pass over K and V in key order: pooled K/V (64-token windows over patch
@@ -113,13 +206,58 @@ __global__ void __launch_bounds__(POOL_NT) pool_kv_kernel(
     const T *__restrict__ k, const T *__restrict__ v, int H, int S, int HW, int Tp, int Tk,
     long long sb, long long sh, long long st, T *__restrict__ kbar, T *__restrict__ vbar,
     uint16_t *__restrict__ v16, float *__restrict__ kpart) {
-    __shared__ float kt[KS_K][65];
-    __shared__ float vt[KS_K][65];
     const int kb = blockIdx.x, bh = blockIdx.y, nkb = gridDim.x;
     const int b = bh / H, h = bh - b * H;
     const int c0 = kb * KS_K, nvalid = min(KS_K, Tk - c0);
     const int npatch = max(0, min(KS_K, Tp - c0));
     const int nkp = (Tp + KS_K - 1) / KS_K;
+    if constexpr (sizeof(T) == 2) {
+        // bf16: raw tiles in shared memory for the column sums; fp16 V from registers
+        __shared__ __align__(16) uint16_t kb16[KS_K][72];
+        __shared__ __align__(16) uint16_t vb16[KS_K][72];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const int i = threadIdx.x + p * POOL_NT;  // 0..1023: K rows then V rows
+            const bool isv = i >= KS_K * 8;
+            const int r = (i >> 3) & 63, c = (i & 7) * 8;
+            uint4 u = make_uint4(0u, 0u, 0u, 0u);
+            if (r < nvalid) {
+                const int cc = c0 + r;
+                const long long tok = cc < Tp ? patch_tok(cc, S, HW) : special_tok(cc - Tp, S, HW);
+                u = *reinterpret_cast<const uint4 *>((isv ? v : k) + b * sb + h * sh + tok * st + c);
+            }
+            *reinterpret_cast<uint4 *>(isv ? &vb16[r][c] : &kb16[r][c]) = u;
+            if (isv && v16 != nullptr && r < nvalid) {
+                const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+                uint32_t w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    __half2 hv = __floats2half2_rn(__uint_as_float(wv[j] << 16), __uint_as_float(wv[j] & 0xFFFF0000u));
+                    w[j] = *reinterpret_cast<uint32_t *>(&hv);
+                }
+                *reinterpret_cast<uint4 *>(v16 + ((size_t)bh * Tk + c0 + r) * HD + c) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+        __syncthreads();
+        const int tid = threadIdx.x;
+        if (kbar != nullptr && kb < nkp && tid < 2 * HD) {
+            const int d = tid & 63;
+            const bool isv = tid >= HD;
+            uint16_t(*src)[72] = isv ? vb16 : kb16;
+            float s = 0.0f;
+            for (int t = 0; t < npatch; ++t) s = __fadd_rn(s, __uint_as_float((uint32_t)src[t][d] << 16));
+            DT<T>::store(isv ? vbar : kbar, ((size_t)bh * nkp + kb) * HD + d, __fdiv_rn(s, (float)npatch));
+        }
+        if (kpart != nullptr && tid >= 2 * HD && tid < 3 * HD) {
+            const int d = tid - 2 * HD;
+            float s = 0.0f;
+            for (int t = 0; t < nvalid; ++t) s = __fadd_rn(s, f16r_from<T>(__uint_as_float((uint32_t)kb16[t][d] << 16)));
+            kpart[((size_t)bh * nkb + kb) * HD + d] = s;
+        }
+        return;
+    }
+    __shared__ float kt[KS_K][65];
+    __shared__ float vt[KS_K][65];
     for (int i = threadIdx.x; i < KS_K * 16; i += POOL_NT) {
         int r = (i >> 3) & 63, c = (i & 7) * 8;
         bool isv = i >= KS_K * 8;
@@ -147,7 +285,7 @@ __global__ void __launch_bounds__(POOL_NT) pool_kv_kernel(
     if (kpart != nullptr && tid >= 2 * HD && tid < 3 * HD) {
         const int d = tid - 2 * HD;
         float s = 0.0f;
-        for (int t = 0; t < nvalid; ++t) s = __fadd_rn(s, f16r(kt[t][d]));
+        for (int t = 0; t < nvalid; ++t) s = __fadd_rn(s, f16r_from<T>(kt[t][d]));
         kpart[((size_t)bh * nkb + kb) * HD + d] = s;
     }
     if (v16 != nullptr) {
@@ -155,8 +293,10 @@ __global__ void __launch_bounds__(POOL_NT) pool_kv_kernel(
             int r = i >> 3, c = (i & 7) * 8;
             uint32_t w[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                w[j] = (uint32_t)f16bits(vt[r][c + 2 * j]) | ((uint32_t)f16bits(vt[r][c + 2 * j + 1]) << 16);
+            for (int j = 0; j < 4; ++j) {
+                __half2 hv = __floats2half2_rn(vt[r][c + 2 * j], vt[r][c + 2 * j + 1]);  // packed: one op per pair
+                w[j] = *reinterpret_cast<uint32_t *>(&hv);
+            }
             *reinterpret_cast<uint4 *>(v16 + ((size_t)bh * Tk + c0 + r) * HD + c) = make_uint4(w[0], w[1], w[2], w[3]);
         }
     }
@@ -180,21 +320,68 @@ __global__ void __launch_bounds__(POOL_NT) kquant_kernel(
     const int kb = blockIdx.x, bh = blockIdx.y, nkb = gridDim.x;
     const int b = bh / H, h = bh - b * H;
     const int c0 = kb * KS_K, nvalid = min(KS_K, Tk - c0);
-    for (int i = threadIdx.x; i < KS_K * 8; i += POOL_NT) {
-        int r = i >> 3, c = (i & 7) * 8;
-        float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (r < nvalid) {
-            int cc = c0 + r;
-            long long tok = cc < Tp ? patch_tok(cc, S, HW) : special_tok(cc - Tp, S, HW);
-            load8<T>(k + b * sb + h * sh + tok * st + c, x);
+    if constexpr (sizeof(T) == 2) {
+        // each thread: 2 x 8 values in registers, fp16(fp16(k) - km) formed in pairs
+        float x[2][8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) x[j] = f16r(__fsub_rn(f16r(x[j]), km[(size_t)bh * HD + c + j]));
+        for (int p = 0; p < 2; ++p) {
+            const int i = threadIdx.x + p * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+            uint4 u = make_uint4(0u, 0u, 0u, 0u);
+            if (r < nvalid) {
+                const int cc = c0 + r;
+                const long long tok = cc < Tp ? patch_tok(cc, S, HW) : special_tok(cc - Tp, S, HW);
+                u = *reinterpret_cast<const uint4 *>(k + b * sb + h * sh + tok * st + c);
+            }
+            const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+            const float *kmr = km + (size_t)bh * HD + c;
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                const float a0 = f16r_from<T>(__uint_as_float(wv[j >> 1] << 16));
+                const float a1 = f16r_from<T>(__uint_as_float(wv[j >> 1] & 0xFFFF0000u));
+                const float2 f = __half22float2(__floats2half2_rn(__fsub_rn(a0, kmr[j]), __fsub_rn(a1, kmr[j + 1])));
+                x[p][j] = r < nvalid ? f.x : 0.0f;
+                x[p][j + 1] = r < nvalid ? f.y : 0.0f;
+            }
         }
+        float amax = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) kt[r][c + j] = x[j];
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[p][j]));
+        amax = block_max_float<POOL_NT>(amax, red);
+        const float sc = __fdiv_rn(amax, 127.0f);
+        const float rc = sc != 0.0f ? __frcp_rn(sc) : 0.0f;
+        if (threadIdx.x == 0) kscale[(size_t)bh * nkb + kb] = sc;
+        int8_t *dst = k8 + ((size_t)bh * Tk + c0) * HD;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            const int i = threadIdx.x + p * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+            if (r >= nvalid) continue;
+            uint32_t w[2] = {0u, 0u};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int qv = sc != 0.0f ? quant_code(div_by(x[p][j], sc, rc)) : 0;
+                w[j >> 2] |= ((uint32_t)(uint8_t)(int8_t)qv) << ((j & 3) * 8);
+            }
+            *reinterpret_cast<uint2 *>(dst + (size_t)r * 64 + c) = make_uint2(w[0], w[1]);
+        }
+    } else {
+        for (int i = threadIdx.x; i < KS_K * 8; i += POOL_NT) {
+            int r = i >> 3, c = (i & 7) * 8;
+            float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (r < nvalid) {
+                int cc = c0 + r;
+                long long tok = cc < Tp ? patch_tok(cc, S, HW) : special_tok(cc - Tp, S, HW);
+                load8<T>(k + b * sb + h * sh + tok * st + c, x);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) x[j] = f16r(__fsub_rn(f16r(x[j]), km[(size_t)bh * HD + c + j]));
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) kt[r][c + j] = x[j];
+        }
+        __syncthreads();
+        quant_tile(kt, nvalid, k8 + ((size_t)bh * Tk + c0) * HD, kscale + (size_t)bh * nkb + kb, red);
     }
-    __syncthreads();
-    quant_tile(kt, nvalid, k8 + ((size_t)bh * Tk + c0) * HD, kscale + (size_t)bh * nkb + kb, red);
 }
 
 // ------------------------------------------------------------------ predict
@@ -507,5 +694,32 @@ extern "C" int ress_hess_adjust(const int32_t *base, const float *scores_norm, i
     const int cols = B * nq, wpb = 8;
     hess_kernel<<<(cols + wpb - 1) / wpb, 32 * wpb, 0, (cudaStream_t)stream>>>(
         base, scores_norm, B, H, nq, max_val, one_minus_beta, beta, max_iters, min_clamp, nts, status);
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}
+
+// ------------------------------------------------------------------ self-check
+namespace ress {
+// Every positive finite fp16 amax (blockIdx.x + 1 as fp16 bits) against every
+// fp16 x with |x| <= amax: the count of quotients where div_by differs from
+// IEEE division by the quantiser's scale RN(amax / 127).
+__global__ void check_division_kernel(int32_t *__restrict__ mismatches) {
+    const uint16_t abits = (uint16_t)(blockIdx.x + 1);
+    const float amax = __half2float(__ushort_as_half(abits));
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float rc = __frcp_rn(sc);
+    int bad = 0;
+    for (uint32_t b = threadIdx.x; b <= abits; b += blockDim.x) {
+        const float x = __half2float(__ushort_as_half((uint16_t)b));
+        // compared as values: -0 and +0 quantise to the same code
+        bad += (div_by(x, sc, rc) != __fdiv_rn(x, sc)) ? 1 : 0;
+        bad += (div_by(-x, sc, rc) != __fdiv_rn(-x, sc)) ? 1 : 0;
+    }
+    if (bad) atomicAdd(mismatches, bad);
+}
+}  // namespace ress
+
+extern "C" int ress_check_scale_division(int32_t *mismatches, ress_stream_t stream) {
+    if (!mismatches) return RESS_E_ARG;
+    ress::check_division_kernel<<<0x7BFF, 256, 0, (cudaStream_t)stream>>>(mismatches);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }

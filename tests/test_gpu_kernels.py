@@ -257,3 +257,18 @@ def test_sparse_attention_random_maps(density):
     e = torch.cat(errs)
     assert e.max().item() < 2e-2, e.max().item()
     assert e.mean().item() < 1e-3, e.mean().item()
+
+
+def test_scale_division_exhaustive():
+    """The quantisers divide by RN(amax/127) with a reciprocal and one fma
+    correction; over every fp16 amax and every fp16 |x| <= amax it must give
+    the IEEE quotient."""
+    import ctypes
+
+    from ress_b200 import _lib
+
+    n = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert _lib.load().ress_check_scale_division(ctypes.c_void_p(n.data_ptr()), stream) == 0
+    torch.cuda.synchronize()
+    assert int(n.item()) == 0
