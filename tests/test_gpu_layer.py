@@ -219,3 +219,31 @@ def test_view_sharded_layer_equals_full(world):
         assert torch.equal(res.counts, ref.counts[ref_rows])
         valid = torch.arange(res.lists.shape[1], device=dev)[None, :] < res.counts[:, None]
         assert torch.equal(torch.where(valid, res.lists, -1), torch.where(valid, ref.lists[ref_rows], -1))
+
+
+def test_da3_shape_layer_matches_oracle():
+    """The DA3 backbone's metadata (backbones.py: 24 heads, one special token)
+    through the same kernels: budgets and keep lists bit-identical to the
+    oracle chained like ress_attention_forward."""
+    shape = synth.LayerShape(n_frames=4, n_heads=24, n_special=1, grid_h=28, grid_w=28)
+    q, k, v = synth.layer_qkv(shape, seed=5, dtype=torch.bfloat16)
+    H = 24
+    M = synth.metric_from_weight(synth.out_proj_weight(dim=H * 64), H)
+    hs = synth.fisher_table(n_heads=H, seed=7)[0, 2]
+    L = K.Layout(1, H, shape.n_frames, shape.n_special, shape.hw)
+    dev = torch.device("cuda", 0)
+    budget = LY.BudgetSpec("hess", sparse_ratio=0.5, scores_norm=K.scores_norm(hs))
+    res = LY.global_layer(q.to(dev), k.to(dev), v.to(dev), L, budget, LY.OrderSpec("restore_swap", M=M.to(dev)))
+    torch.cuda.synchronize()
+    K.check_status(dev)
+    qp, _ = synth.split_tokens(q, shape)
+    kp, ks = synth.split_tokens(k, shape)
+    vp, _ = synth.split_tokens(v, shape)
+    o = oracle.layer_select(qp, kp, vp, ks.shape[-2], M, head_scores=hs, mode="ress", sparse_ratio=0.5,
+                            cdf_threshold=None)
+    assert torch.equal(res.nts.cpu(), o["nts"])
+    assert torch.equal(res.counts.cpu(), o["counts"])
+    lists = res.lists.cpu()
+    for i in range(o["counts"].numel()):
+        c = int(o["counts"][i])
+        assert torch.equal(lists[i, :c], o["lists"][i, :c]), i
