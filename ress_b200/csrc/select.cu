@@ -474,6 +474,19 @@ __global__ void __launch_bounds__(SEL_NT) map_lists_kernel(const uint8_t *__rest
 // restore_swap_kernel / the oracle; only the placement of data changes.
 constexpr int G_NT = 64;
 
+// (d0, d1) = (a0 * b + c0, a1 * b + c1): two independent IEEE fp32 FMAs in one
+// issue slot (fma.rn.f32x2); each chain gets exactly the bits of __fmaf_rn.
+__device__ __forceinline__ void fma2_chain(float &c0, float &c1, float a0, float a1, float b) {
+    asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %4};\n\t"
+        "mov.b64 rc, {%0, %1};\n\t"
+        "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rc;\n\t}"
+        : "+f"(c0), "+f"(c1)
+        : "f"(a0), "f"(a1), "f"(b));
+}
+
 __device__ __forceinline__ void gbar(int g) { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(G_NT) : "memory"); }
 
 struct GroupScratch {
@@ -728,12 +741,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     }
     gbar(g);
     const float eps4 = bf16r(1e-4f);
-    for (int k = t; k < n_cand; k += G_NT) {
-        float v[HD];
-        vb_row(vb, k, v);
-        float acc = 0.0f;
-#pragma unroll
-        for (int i = 0; i < HD; ++i) acc = __fmaf_rn(S.Mvq[i], v[i], acc);
+    auto cut = [&](int k, float acc) {
         const float cross = bf16r(acc);
         float quad = bf16r(__fsub_rn(S.tqs, bf16r(__fmul_rn(2.0f, cross))));
         quad = bf16r(__fadd_rn(quad, tk[(size_t)bh * n_cand + k]));
@@ -745,6 +753,28 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
         if (s_out) s_out[(size_t)row * n_cand + k] = bf16bits(sv);
         key[k] = order_key(bf16r(__fdiv_rn(sv, den)));
         valid[k] = 1;
+    };
+    {
+        // two candidates per step: two FMA chains in one packed instruction
+        int k = t;
+        for (; k + G_NT < n_cand; k += 2 * G_NT) {
+            float v0[HD], v1[HD];
+            vb_row(vb, k, v0);
+            vb_row(vb, k + G_NT, v1);
+            float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < HD; ++i) fma2_chain(a0, a1, v0[i], v1[i], S.Mvq[i]);
+            cut(k, a0);
+            cut(k + G_NT, a1);
+        }
+        if (k < n_cand) {
+            float v0[HD];
+            vb_row(vb, k, v0);
+            float a0 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < HD; ++i) a0 = __fmaf_rn(S.Mvq[i], v0[i], a0);
+            cut(k, a0);
+        }
     }
     gbar(g);
     const int nt = nts[row];
@@ -795,11 +825,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
             vb_row(vb, k + G_NT, v1);
             float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-            for (int j = 0; j < HD; ++j) {
-                const float mj = S.Mgb[j];
-                a0 = __fmaf_rn(v0[j], mj, a0);
-                a1 = __fmaf_rn(v1[j], mj, a1);
-            }
+            for (int j = 0; j < HD; ++j) fma2_chain(a0, a1, v0[j], v1[j], S.Mgb[j]);
             quality(k, a0);
             quality(k + G_NT, a1);
         }
