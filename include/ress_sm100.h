@@ -259,6 +259,17 @@ int ress_sparse_attn(const int8_t *q8, const float *qscale, const int8_t *k8, co
                      long long out_sh, long long out_st, int out_hw, int out_special,
                      int32_t *status, ress_stream_t stream);
 
+/* ress_sparse_attn with a launch schedule: row_order (device int32, one entry
+ * per (head, q-block) row, caller-allocated scratch) is filled with the rows
+ * in descending kept-block count and the attention CTAs take rows in that
+ * order, so the longest rows start first and the last wave is short.  Same
+ * outputs, bit for bit.  Widths above 16384 fall back to the plain order. */
+int ress_sparse_attn_sched(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
+                           const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
+                           const int32_t *counts, int list_width, float sm_scale, float *out,
+                           long long out_sh, long long out_st, int out_hw, int out_special,
+                           int32_t *status, int32_t *row_order, ress_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,6 +50,8 @@ SIGNATURES = {
     "ress_map_to_lists": (_I, [_P, _I, _I, _P, _P, _I, _P, _P]),
     "ress_sparse_attn": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _I, _F, _P, _L, _L, _I,
                               _I, _P, _P]),
+    "ress_sparse_attn_sched": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _I, _F, _P, _L, _L, _I,
+                                    _I, _P, _P, _P]),
 }
 
 _lib = None

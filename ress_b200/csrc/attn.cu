@@ -331,7 +331,8 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     const __grid_constant__ CUtensorMap tm_v, const float *__restrict__ qscale,
     const float *__restrict__ kscale, int nqb, int nkb, int Tq, int Tk, const int32_t *__restrict__ lists,
     const int32_t *__restrict__ counts, int list_width, float sm_scale_log2, float *__restrict__ out,
-    long long out_sh, long long out_st, int out_hw, int out_special, int32_t *__restrict__ status) {
+    long long out_sh, long long out_st, int out_hw, int out_special, int32_t *__restrict__ status,
+    const int32_t *__restrict__ row_order) {
     extern __shared__ unsigned char dyn_raw[];
     __shared__ Bars B;
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)dyn_raw + 1023) & ~(uintptr_t)1023);
@@ -347,7 +348,9 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x;
+    // rows in descending block count when an order is given: the long rows of
+    // heavily budgeted heads start first and the last wave is short
+    const int row = row_order != nullptr ? row_order[blockIdx.x] : (int)blockIdx.x;
     const int bh = row / nqb, qb = row - bh * nqb;
     const int cnt = min(counts[row], list_width);
     const int32_t *lst = lists + (size_t)row * list_width;
@@ -599,6 +602,31 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
 }
 
+// Rows sorted by descending count (counting sort, one CTA; ties in any
+// order: a row's output does not depend on which CTA computes it).
+constexpr int ORDER_NT = 1024;
+constexpr int ORDER_MAX_WIDTH = 16384;
+__global__ void __launch_bounds__(ORDER_NT) row_order_kernel(const int32_t *__restrict__ counts, int rows,
+                                                              int list_width, int32_t *__restrict__ order) {
+    extern __shared__ int pos[];  // list_width + 1 bins
+    const int nb = list_width + 1;
+    for (int c = threadIdx.x; c < nb; c += ORDER_NT) pos[c] = 0;
+    __syncthreads();
+    for (int r = threadIdx.x; r < rows; r += ORDER_NT) atomicAdd(&pos[min(max(counts[r], 0), list_width)], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int c = list_width; c >= 0; --c) {  // descending: largest counts first
+            const int n = pos[c];
+            pos[c] = acc;
+            acc += n;
+        }
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < rows; r += ORDER_NT)
+        order[atomicAdd(&pos[min(max(counts[r], 0), list_width)], 1)] = r;
+}
+
 // ------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -630,11 +658,11 @@ static bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, i
 
 using namespace ress;
 
-extern "C" int ress_sparse_attn(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
-                                const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
-                                const int32_t *counts, int list_width, float sm_scale, float *out,
-                                long long out_sh, long long out_st, int out_hw, int out_special,
-                                int32_t *status, ress_stream_t stream) {
+static int sparse_attn_impl(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
+                            const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
+                            const int32_t *counts, int list_width, float sm_scale, float *out, long long out_sh,
+                            long long out_st, int out_hw, int out_special, int32_t *status, int32_t *row_order,
+                            ress_stream_t stream) {
     if (!q8 || !qscale || !k8 || !kscale || !v16 || !lists || !counts || !out || !status) return RESS_E_ARG;
     if (BH <= 0 || Tq <= 0 || Tk <= 0 || list_width <= 0 || out_hw <= 0 || out_special < 0) return RESS_E_ARG;
     if (((uintptr_t)q8 | (uintptr_t)k8 | (uintptr_t)v16) & 15) return RESS_E_ARG;
@@ -646,10 +674,37 @@ extern "C" int ress_sparse_attn(const int8_t *q8, const float *qscale, const int
         !attn::make_map(&tv, v16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Tk, BH, 64, CU_TENSOR_MAP_SWIZZLE_128B))
         return RESS_E_NO_DEVICE;
     const int nqb = (Tq + 127) / 128, nkb = (Tk + 63) / 64;
+    const int rows = BH * nqb;
+    if (row_order != nullptr && list_width <= attn::ORDER_MAX_WIDTH) {
+        const size_t sm = (size_t)(list_width + 1) * sizeof(int);
+        set_smem_attr((const void *)attn::row_order_kernel, sm);
+        attn::row_order_kernel<<<1, attn::ORDER_NT, sm, (cudaStream_t)stream>>>(counts, rows, list_width, row_order);
+    } else {
+        row_order = nullptr;
+    }
     set_smem_attr((const void *)attn::sparse_attn_kernel, attn::SMEM_BYTES);
     const float log2e = 1.4426950408889634f;
-    attn::sparse_attn_kernel<<<BH * nqb, attn::NT, attn::SMEM_BYTES, (cudaStream_t)stream>>>(
+    attn::sparse_attn_kernel<<<rows, attn::NT, attn::SMEM_BYTES, (cudaStream_t)stream>>>(
         tq, tk, tv, qscale, kscale, nqb, nkb, Tq, Tk, lists, counts, list_width, sm_scale * log2e, out, out_sh,
-        out_st, out_hw, out_special, status);
+        out_st, out_hw, out_special, status, row_order);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}
+
+extern "C" int ress_sparse_attn(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
+                                const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
+                                const int32_t *counts, int list_width, float sm_scale, float *out,
+                                long long out_sh, long long out_st, int out_hw, int out_special,
+                                int32_t *status, ress_stream_t stream) {
+    return sparse_attn_impl(q8, qscale, k8, kscale, v16, BH, Tq, Tk, lists, counts, list_width, sm_scale, out,
+                            out_sh, out_st, out_hw, out_special, status, nullptr, stream);
+}
+
+extern "C" int ress_sparse_attn_sched(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
+                                      const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
+                                      const int32_t *counts, int list_width, float sm_scale, float *out,
+                                      long long out_sh, long long out_st, int out_hw, int out_special,
+                                      int32_t *status, int32_t *row_order, ress_stream_t stream) {
+    if (!row_order) return RESS_E_ARG;
+    return sparse_attn_impl(q8, qscale, k8, kscale, v16, BH, Tq, Tk, lists, counts, list_width, sm_scale, out,
+                            out_sh, out_st, out_hw, out_special, status, row_order, stream);
 }

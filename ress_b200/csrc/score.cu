@@ -199,6 +199,12 @@ __global__ void __launch_bounds__(POOL_NT) pool_q_kernel(
     }
 }
 
+template <typename T>
+__device__ __forceinline__ void pool_kv_generic(const T *__restrict__ k, const T *__restrict__ v, int H, int S, int HW,
+                                                int Tp, int Tk, long long sb, long long sh, long long st,
+                                                T *__restrict__ kbar, T *__restrict__ vbar, uint16_t *__restrict__ v16,
+                                                float *__restrict__ kpart);
+
 // Pass over K and V in key order: pooled K/V (64-token windows over patch
 // tokens), fp16 V, and per-block fp16 sums of K for the key mean.
 template <typename T>
@@ -254,8 +260,22 @@ __global__ void __launch_bounds__(POOL_NT) pool_kv_kernel(
             for (int t = 0; t < nvalid; ++t) s = __fadd_rn(s, f16r_from<T>(__uint_as_float((uint32_t)kb16[t][d] << 16)));
             kpart[((size_t)bh * nkb + kb) * HD + d] = s;
         }
-        return;
+    } else {
+        pool_kv_generic<T>(k, v, H, S, HW, Tp, Tk, sb, sh, st, kbar, vbar, v16, kpart);
     }
+}
+
+// fp32 input: fp32 tiles in shared memory.
+template <typename T>
+__device__ __forceinline__ void pool_kv_generic(const T *__restrict__ k, const T *__restrict__ v, int H, int S, int HW,
+                                                int Tp, int Tk, long long sb, long long sh, long long st,
+                                                T *__restrict__ kbar, T *__restrict__ vbar, uint16_t *__restrict__ v16,
+                                                float *__restrict__ kpart) {
+    const int kb = blockIdx.x, bh = blockIdx.y, nkb = gridDim.x;
+    const int b = bh / H, h = bh - b * H;
+    const int c0 = kb * KS_K, nvalid = min(KS_K, Tk - c0);
+    const int npatch = max(0, min(KS_K, Tp - c0));
+    const int nkp = (Tp + KS_K - 1) / KS_K;
     __shared__ float kt[KS_K][65];
     __shared__ float vt[KS_K][65];
     for (int i = threadIdx.x; i < KS_K * 16; i += POOL_NT) {

@@ -360,7 +360,8 @@ def lists_to_map(lists, counts, width):
     return m[:, :width]
 
 
-def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout=None, sm_scale=None):
+def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout=None, sm_scale=None,
+                schedule=True):
     """Block-sparse attention.  q8 (BH, Tq, 64); k8/v16 (BH, Tk, 64).
     out: fp32 tensor; with out_layout (a Layout) rows land at their full-layout
     positions of a (B, H, frames*(special+hw), 64) tensor."""
@@ -383,6 +384,14 @@ def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(HD)
     lw = lists.shape[-1]
+    if schedule:
+        # rows launched in descending kept-block count (same bits as the plain order)
+        order = torch.empty(counts.numel(), dtype=torch.int32, device=dev)
+        check(_lib.load().ress_sparse_attn_sched(_ptr(q8), _ptr(qscale), _ptr(k8), _ptr(kscale), _ptr(v16), BH, Tq,
+                                                 Tk, _ptr(lists), _ptr(counts), lw, ctypes.c_float(sm_scale), _ptr(out),
+                                                 o_sh, o_st, o_hw, o_sp, _ptr(status_word(dev)), _ptr(order),
+                                                 _stream(dev)), "ress_sparse_attn_sched")
+        return out
     check(_lib.load().ress_sparse_attn(_ptr(q8), _ptr(qscale), _ptr(k8), _ptr(kscale), _ptr(v16), BH, Tq, Tk,
                                        _ptr(lists), _ptr(counts), lw, ctypes.c_float(sm_scale), _ptr(out), o_sh, o_st,
                                        o_hw, o_sp, _ptr(status_word(dev)), _stream(dev)), "ress_sparse_attn")

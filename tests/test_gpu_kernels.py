@@ -272,3 +272,14 @@ def test_scale_division_exhaustive():
     assert _lib.load().ress_check_scale_division(ctypes.c_void_p(n.data_ptr()), stream) == 0
     torch.cuda.synchronize()
     assert int(n.item()) == 0
+
+
+def test_scheduled_attention_equals_plain_order():
+    """Rows launched in descending kept-block count give the same bits as the
+    plain row order (each row's result does not depend on its CTA)."""
+    L, q8, qs, k8, ks, v16, sel = _attn_case(SMALL, torch.bfloat16, 0.5)
+    a = K.sparse_attn(q8, qs, k8, ks, v16, sel["lists"], sel["counts"], schedule=False)
+    b = K.sparse_attn(q8, qs, k8, ks, v16, sel["lists"], sel["counts"], schedule=True)
+    torch.cuda.synchronize()
+    K.check_status()
+    assert torch.equal(a, b)
