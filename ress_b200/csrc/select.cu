@@ -913,6 +913,17 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
         const size_t rowb = rs2_row_bytes(nkp, n_cand);
         int R = 8;
         while (R > 0 && fixed + (size_t)R * rowb > 220 * 1024) --R;
+        // few rows (a head split over many GPUs): when the CTAs would not fill
+        // the SMs once, take fewer rows per CTA so that they cover every SM;
+        // a row runs faster with fewer rows sharing its SM.  (Measured: with a
+        // full wave or more, the largest R that fits is fastest.)
+        static int n_sm[64] = {0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev >= 0 && dev < 64 && n_sm[dev] == 0) cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev);
+        const int sms = (dev >= 0 && dev < 64 && n_sm[dev] > 0) ? n_sm[dev] : 148;
+        if (R >= 2 && (long long)BH * ((nq + R - 1) / R) < sms)
+            while (R > 2 && (long long)BH * ((nq + R - 2) / (R - 1)) <= sms) --R;
         if (R >= 2) {
             const size_t sm2 = fixed + (size_t)R * rowb;
             auto k2 = restore_swap_v2_kernel<T>;
