@@ -112,66 +112,95 @@ __device__ __forceinline__ void load_row64(const uint16_t *src, float *v) {
     }
 }
 
-// Rows of vbar per shared-memory stage of the drift chains (two stages,
-// filled with cp.async while the previous one is consumed).
-constexpr int DCH = 64;
-constexpr int STAGE_BYTES = 2 * DCH * HD * 2;
+// Rows of vbar per shared-memory stage of the drift chains: DSTAGES stages
+// in a ring, filled with cp.async DSTAGES - 1 chunks ahead of the chain (the
+// lead covers the L2 latency; measured: one 64-row chunk ahead left the
+// chain waiting on every chunk).
+constexpr int DCH = 32;
+constexpr int DSTAGES = 8;
+constexpr int STAGE_BYTES = DSTAGES * DCH * HD * 2;
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_lead() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(DSTAGES - 1) : "memory");
+}
 
 // acc[d] = sum_k w(k) * vbar[k][d] for d = tid < 64 as one sequential fp32
 // FMA chain per dimension in k order (with w(k) = +0 for masked entries,
 // which leaves the chain bit-for-bit unchanged: it starts at +0 and never
 // reaches -0), and total = sequential fp32 sum of w(k) (thread 64).  vbar
-// rows stream through two shared-memory stages of DCH rows loaded by the
-// whole CTA with cp.async.  mask == nullptr: w(k) = P[k] for all n entries.
-__device__ void rs_chain(const float *P, const uint8_t *mask, const uint16_t *vb, int n, uint16_t *stage,
+// rows stream through a ring of shared-memory stages of DCH rows loaded by
+// the whole CTA with cp.async.  MASKED: w(k) = mask[k] ? P[k] : +0, else
+// P[k].  P (bf16 bits) is 16-byte aligned and mask 8-byte aligned: eight
+// weights come in one 16-byte and one 8-byte load, so the loads of a batch
+// overlap instead of each waiting on the mask byte before it.
+template <bool MASKED>
+__device__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t *vb, int n, uint16_t *stage,
                          float &acc_out, float &total_out) {
     const int tid = threadIdx.x;
     const int nch = (n + DCH - 1) / DCH;
     auto issue = [&](int c) {
         const int r0 = c * DCH, rows = min(DCH, n - r0);
-        uint16_t *dst = stage + (c & 1) * DCH * HD;
+        uint16_t *dst = stage + (c % DSTAGES) * DCH * HD;
         for (int i = tid; i < rows * 8; i += SEL_NT)
             cp_async16(dst + i * 8, vb + (size_t)r0 * HD + (size_t)i * 8);
     };
+    auto weights8 = [&](int k0, float (&w)[8]) {
+        const uint4 pw = *reinterpret_cast<const uint4 *>(P + k0);
+        const uint32_t p4[4] = {pw.x, pw.y, pw.z, pw.w};
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            w[u] = __uint_as_float(u & 1 ? (p4[u >> 1] & 0xFFFF0000u) : (p4[u >> 1] << 16));
+        if constexpr (MASKED) {
+            const uint2 mw = *reinterpret_cast<const uint2 *>(mask + k0);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t byte = ((u < 4 ? mw.x : mw.y) >> ((u & 3) * 8)) & 0xFFu;
+                w[u] = byte ? w[u] : 0.0f;
+            }
+        }
+    };
+    auto weight1 = [&](int k) -> float {
+        const float p = bf16_from_bits(P[k]);
+        if constexpr (MASKED) return mask[k] ? p : 0.0f;
+        return p;
+    };
     float acc = 0.0f, tot = 0.0f;
-    issue(0);
-    cp_async_commit();
-    for (int c = 0; c < nch; ++c) {
-        if (c + 1 < nch) issue(c + 1);
+    for (int c = 0; c < DSTAGES - 1; ++c) {
+        if (c < nch) issue(c);
         cp_async_commit();
-        cp_async_wait1();
-        __syncthreads();
+    }
+    for (int c = 0; c < nch; ++c) {
+        if (c + DSTAGES - 1 < nch) issue(c + DSTAGES - 1);
+        cp_async_commit();
+        cp_async_wait_lead();  // chunk c has landed (this thread's copies)
+        __syncthreads();       // ... and every thread's
         const int r0 = c * DCH, rows = min(DCH, n - r0);
-        const uint16_t *st = stage + (c & 1) * DCH * HD;
+        const uint16_t *st = stage + (c % DSTAGES) * DCH * HD;
         if (tid < HD) {
             int r = 0;
             for (; r + 8 <= rows; r += 8) {
                 float w[8], v[8];
+                weights8(r0 + r, w);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int k = r0 + r + u;
-                    w[u] = (mask == nullptr || mask[k]) ? P[k] : 0.0f;
-                    v[u] = bf16_from_bits(st[(r + u) * HD + tid]);
-                }
+                for (int u = 0; u < 8; ++u) v[u] = bf16_from_bits(st[(r + u) * HD + tid]);
 #pragma unroll
                 for (int u = 0; u < 8; ++u) acc = __fmaf_rn(w[u], v[u], acc);
             }
-            for (; r < rows; ++r) {
-                const int k = r0 + r;
-                acc = __fmaf_rn((mask == nullptr || mask[k]) ? P[k] : 0.0f, bf16_from_bits(st[r * HD + tid]), acc);
-            }
+            for (; r < rows; ++r) acc = __fmaf_rn(weight1(r0 + r), bf16_from_bits(st[r * HD + tid]), acc);
         } else if (tid == HD) {
-            for (int r = 0; r < rows; ++r) {
-                const int k = r0 + r;
-                tot = __fadd_rn(tot, (mask == nullptr || mask[k]) ? P[k] : 0.0f);
+            int r = 0;
+            for (; r + 8 <= rows; r += 8) {
+                float w[8];
+                weights8(r0 + r, w);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) tot = __fadd_rn(tot, w[u]);
             }
+            for (; r < rows; ++r) tot = __fadd_rn(tot, weight1(r0 + r));
         }
         __syncthreads();
     }
@@ -181,11 +210,11 @@ __device__ void rs_chain(const float *P, const uint8_t *mask, const uint16_t *vb
 
 // g, Mg, G = ||g||^2_M and K for the current drop set (projected.py:868-878,
 // 908-920).  vb: bf16 bits (nkp, 64) of this head.  S.Mt holds M transposed.
-__device__ void rs_drift(RSShared &S, const float *P, const uint8_t *drop, const uint16_t *vb,
+__device__ void rs_drift(RSShared &S, const uint16_t *P, const uint8_t *drop, const uint16_t *vb,
                          int n_cand, uint16_t *stage) {
     const int tid = threadIdx.x;
     float acc, tot;
-    rs_chain(P, drop, vb, n_cand, stage, acc, tot);
+    rs_chain<true>(P, drop, vb, n_cand, stage, acc, tot);
     if (tid < HD) S.g[tid] = bf16r(acc);  // masked_vbar_d, finished below
     else if (tid == HD) S.sum_pd = bf16r(tot);
     __syncthreads();
@@ -220,11 +249,13 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     const int row = blockIdx.x;
     const int bh = row / nq, h = bh % H;
     const int tid = threadIdx.x;
-    uint16_t *stage = reinterpret_cast<uint16_t *>(dyn);       // 2 x DCH x 64 bf16
-    float *P = reinterpret_cast<float *>(dyn + STAGE_BYTES);   // nkp
-    float *ssq = P + nkp;                                      // n_cand
-    uint32_t *key = reinterpret_cast<uint32_t *>(ssq + n_cand); // n_cand
-    uint8_t *drop = reinterpret_cast<uint8_t *>(key + n_cand);   // n_cand each
+    // P and s^2 hold bf16-rounded values: kept as bf16 bits (exact), which
+    // leaves room for the deep vbar stage ring
+    uint16_t *stage = reinterpret_cast<uint16_t *>(dyn);                // DSTAGES x DCH x 64 bf16
+    uint16_t *P = reinterpret_cast<uint16_t *>(dyn + STAGE_BYTES);      // nkp bf16
+    uint16_t *ssq = P + ((nkp + 7) & ~7);                               // n_cand bf16
+    uint32_t *key = reinterpret_cast<uint32_t *>(ssq + ((n_cand + 7) & ~7)); // n_cand (padded to 16 B)
+    uint8_t *drop = reinterpret_cast<uint8_t *>(key + ((n_cand + 3) & ~3)); // n_cand each; drop 16-B aligned
     uint8_t *best = drop + n_cand;
     uint8_t *valid = best + n_cand;
     uint8_t *sel = valid + n_cand;
@@ -232,12 +263,12 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     const uint16_t *vb = vb16 + (size_t)bh * nkp * HD;
 
     for (int i = tid; i < HD * HD; i += SEL_NT) S.Mt[(i & (HD - 1)) * HD + (i >> 6)] = M[(size_t)h * HD * HD + i];
-    for (int k = tid; k < nkp; k += SEL_NT) P[k] = bf16r(DT<T>::load(attn, (size_t)row * nkp + k));
+    for (int k = tid; k < nkp; k += SEL_NT) P[k] = bf16bits(DT<T>::load(attn, (size_t)row * nkp + k));
     __syncthreads();
     // dense_reference over all pooled blocks: v_bar_query = P @ v_bar, total = sum(P)
     {
         float acc, tot;
-        rs_chain(P, nullptr, vb, nkp, stage, acc, tot);
+        rs_chain<false>(P, nullptr, vb, nkp, stage, acc, tot);
         if (tid < HD) S.vq[tid] = bf16r(acc);
         else if (tid == HD) S.tm = bf16r(tot);
     }
@@ -268,10 +299,11 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
         quad = bf16r(__fadd_rn(quad, tk[(size_t)bh * n_cand + k]));
         quad = clamp_min(quad, 0.0f);
         float sq = bf16r(__fsqrt_rn(quad));
-        float s = bf16r(__fmul_rn(P[k], sq));
-        float den = clamp_min(bf16r(__fsub_rn(1.0f, P[k])), eps4);
+        const float pk = bf16_from_bits(P[k]);
+        float s = bf16r(__fmul_rn(pk, sq));
+        float den = clamp_min(bf16r(__fsub_rn(1.0f, pk)), eps4);
         float s_cut = bf16r(__fdiv_rn(s, den));
-        ssq[k] = bf16r(__fmul_rn(s, s));
+        ssq[k] = bf16bits(__fmul_rn(s, s));
         if (s_out) s_out[(size_t)row * n_cand + k] = bf16bits(s);
         key[k] = order_key(s_cut);
         valid[k] = 1;
@@ -310,14 +342,15 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
 #pragma unroll
             for (int j = 0; j < HD; ++j) acc = __fmaf_rn(v[j], S.Mgb[j], acc);
             float tkk = bf16r(acc);
-            float r = bf16r(__fmul_rn(P[k], bf16r(__fsub_rn(tkk, tqb))));
+            const float pk = bf16_from_bits(P[k]), sk = bf16_from_bits(ssq[k]);
+            float r = bf16r(__fmul_rn(pk, bf16r(__fsub_rn(tkk, tqb))));
             if (drop[k]) {
-                float rq = knorm_quality(G, K, __fadd_rn(__fmul_rn(2.0f, r), ssq[k]), P[k]);
+                float rq = knorm_quality(G, K, __fadd_rn(__fmul_rn(2.0f, r), sk), pk);
                 key[k] = order_key(rq);
                 ben |= (rq > 0.0f) ? 1 : 0;
                 ++nd;
             } else {
-                float cq = knorm_quality(G, K, __fsub_rn(ssq[k], __fmul_rn(2.0f, r)), -P[k]);
+                float cq = knorm_quality(G, K, __fsub_rn(sk, __fmul_rn(2.0f, r)), -pk);
                 key[k] = order_key(cq);
                 ++nk;
             }
@@ -890,7 +923,8 @@ static size_t rs2_row_bytes(int nkp, int n_cand) {
 }
 
 static size_t rs_smem(int nkp, int n_cand) {
-    return (size_t)STAGE_BYTES + (size_t)nkp * 4 + (size_t)n_cand * (4 + 4 + 5);
+    return (size_t)STAGE_BYTES + (size_t)((nkp + 7) & ~7) * 2 + (size_t)((n_cand + 7) & ~7) * 2 +
+           (size_t)((n_cand + 3) & ~3) * 4 + (size_t)n_cand * 5;
 }
 
 template <typename T>
