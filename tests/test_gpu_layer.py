@@ -15,6 +15,7 @@ from ress_b200 import synth
 pytestmark = pytest.mark.gpu
 
 CASES = [
+    ("1f-bf16-ress", synth.LayerShape(n_frames=1), torch.bfloat16, "ress", 0.5, None),
     ("cfg1", synth.CONFIG1, torch.float32, "ress", 0.1, None),
     ("cfg1-hess-cdf", synth.CONFIG1, torch.float32, "prob", 0.5, 0.97),
     ("6f-bf16-ress", synth.LayerShape(n_frames=6), torch.bfloat16, "ress", 0.5, None),
