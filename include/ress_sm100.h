@@ -67,6 +67,18 @@ int ress_version(void);
  * |x| <= amax, whose quotient x / RN(amax/127) the quantisers' reciprocal-
  * and-correction division rounds differently from IEEE division. */
 int ress_check_scale_division(int32_t *mismatches, ress_stream_t stream);
+
+/* Replaces the q/k/v prologue of compute_patch_qkv (src/ress/models/qkv.py:
+ * 25-68) in one pass.  qkv: the fused qkv Linear's output, (B, T, 3, H, 64)
+ * contiguous, RESS_F32 or RESS_BF16.  q/k LayerNorm over the 64 head dims
+ * (fp32 weights and biases, NULL for no affine), then, when rope_cos is
+ * given, the 2-D rotary embedding with the model's (rope_len, 32) cos/sin
+ * tables in the input dtype indexed by pos (B, T, 2) int64 (row, column
+ * position).  Writes q, k, v as (B, H, T, 64) contiguous in the input dtype. */
+int ress_qkv_prologue(const void *qkv, int dtype, int B, int T, int H, const float *qn_weight,
+                      const float *qn_bias, const float *kn_weight, const float *kn_bias, float eps,
+                      const long long *pos, const void *rope_cos, const void *rope_sin, int rope_len,
+                      void *q, void *k, void *v, ress_stream_t stream);
 const char *ress_error_string(int code);
 
 /*

@@ -12,7 +12,8 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-SRC = [os.path.join(HERE, "csrc", f) for f in ("capi.cu", "score.cu", "select.cu", "attn.cu", "noalloc.cu")]
+SRC = [os.path.join(HERE, "csrc", f) for f in ("capi.cu", "score.cu", "select.cu", "attn.cu", "noalloc.cu",
+                                                "prologue.cu")]
 OUT = os.path.join(HERE, "libress_sm100.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [

@@ -396,3 +396,28 @@ def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout
                                        _ptr(lists), _ptr(counts), lw, ctypes.c_float(sm_scale), _ptr(out), o_sh, o_st,
                                        o_hw, o_sp, _ptr(status_word(dev)), _stream(dev)), "ress_sparse_attn")
     return out
+
+
+def qkv_prologue(qkv, H, qn_weight=None, qn_bias=None, kn_weight=None, kn_bias=None, eps=1e-5, pos=None,
+                 rope_cos=None, rope_sin=None):
+    """(B, T, 3*H*64) qkv Linear output -> q, k, v (B, H, T, 64): q/k LayerNorm
+    (fp32 weights) and the optional 2-D rotary embedding in one pass."""
+    _dev_ok(qkv)
+    B, T, C3 = qkv.shape
+    if C3 != 3 * H * HD or not qkv.is_contiguous():
+        raise RessError("qkv must be contiguous (B, T, 3*H*64)")
+    dev = qkv.device
+    q, k, v = (torch.empty(B, H, T, HD, dtype=qkv.dtype, device=dev) for _ in range(3))
+    f32 = lambda t: None if t is None else t.detach().to(device=dev, dtype=torch.float32).contiguous()
+    qw, qb, kw, kb = f32(qn_weight), f32(qn_bias), f32(kn_weight), f32(kn_bias)
+    rope_len = 0
+    if rope_cos is not None:
+        rope_cos, rope_sin = rope_cos.contiguous(), rope_sin.contiguous()
+        if rope_cos.dtype != qkv.dtype or rope_cos.shape[-1] != 32:
+            raise RessError("rotary tables must be (max_pos, 32) in the qkv dtype")
+        rope_len = rope_cos.shape[0]
+        pos = pos.to(dtype=torch.int64).contiguous()
+    check(_lib.load().ress_qkv_prologue(_ptr(qkv), _dtype_code(qkv.dtype), B, T, H, _ptr(qw), _ptr(qb), _ptr(kw),
+                                        _ptr(kb), ctypes.c_float(eps), _ptr(pos), _ptr(rope_cos), _ptr(rope_sin),
+                                        rope_len, _ptr(q), _ptr(k), _ptr(v), _stream(dev)), "ress_qkv_prologue")
+    return q, k, v

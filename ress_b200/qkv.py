@@ -26,12 +26,46 @@ def layer_shape(x, pos, num_special_tokens=5, num_heads=16, shape=None):
     return {"B": B, "N": N, "P": P, "head_dim": C // num_heads, "num_heads": num_heads, "H": H, "W": W, "S": S}
 
 
+def _fusable_norm(m, hd):
+    return (isinstance(m, torch.nn.LayerNorm) and tuple(m.normalized_shape) == (hd,) and m.elementwise_affine
+            and m.bias is not None)
+
+
+def _fused_prologue(self, qkv, pos, nh, hd):
+    """q, k, v from the sm_100a prologue kernel when the block's norms and
+    rotary embedding are ones it reproduces (64-dim affine LayerNorm; this
+    package's 2-D table RoPE or none), else None (torch path below)."""
+    if not qkv.is_cuda or qkv.dtype not in (torch.float32, torch.bfloat16) or hd != 64:
+        return None
+    if torch.is_autocast_enabled() or not (_fusable_norm(self.q_norm, hd) and _fusable_norm(self.k_norm, hd)):
+        return None
+    rope = getattr(self, "rope", None)
+    cos = sin = None
+    if rope is not None:
+        from .vggt import RotaryPosition2D
+
+        if type(rope) is not RotaryPosition2D or pos is None:
+            return None
+        cos, sin = rope._cos_sin(hd // 2, rope.MAX_POS, qkv.device, qkv.dtype)
+    if self.q_norm.eps != self.k_norm.eps:
+        return None
+    from . import kernels as K
+
+    return K.qkv_prologue(qkv.contiguous(), nh, self.q_norm.weight, self.q_norm.bias, self.k_norm.weight,
+                          self.k_norm.bias, eps=self.q_norm.eps, pos=pos, rope_cos=cos, rope_sin=sin)
+
+
 def compute_qkv(self, x, pos, num_special_tokens=5, num_heads=16, shape=None):
     """q, k, v as (B, nh, N*P, hd) views/tensors plus the shape dict."""
     shp = layer_shape(x, pos, num_special_tokens, num_heads, shape)
     B, NP, C = x.shape
     nh, hd = num_heads, C // num_heads
-    qkv = self.qkv(x).view(B, NP, 3, nh, hd).permute(2, 0, 3, 1, 4)
+    lin = self.qkv(x)
+    fused = _fused_prologue(self, lin, pos, nh, hd)
+    if fused is not None:
+        q, k, v = fused
+        return q, k, v, shp
+    qkv = lin.view(B, NP, 3, nh, hd).permute(2, 0, 3, 1, 4)
     q, k, v = qkv.unbind(0)
     q, k = self.q_norm(q), self.k_norm(k)
     if getattr(self, "rope", None) is not None:
