@@ -114,6 +114,91 @@ __device__ __forceinline__ float div_by(float x, float d, float r) {
     return __fmaf_rn(rem, r, q);
 }
 
+// -------------------------------------------------------- invariant division
+// n / d for a divisor fixed per launch, by multiply-high (T. Granlund and
+// P. Montgomery, "Division by invariant integers using multiplication",
+// PLDI 1994): with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// n / d = (umulhi(n, m) + n) >> l for 0 <= n < 2^31.
+struct FastDiv {
+    uint32_t d, m, l;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f{d, 0u, 0u};
+    if (d <= 1) return f;
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    f.m = (uint32_t)((((1ull << 32) * ((1ull << l) - d)) / d) + 1);
+    f.l = l;
+    return f;
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
+    return f.d <= 1 ? n : (__umulhi(n, f.m) + n) >> f.l;
+}
+
+// ------------------------------------------------------------ packed fp32
+// Two fp32 lanes per instruction (sm_100 .f32x2 forms); each lane rounds
+// exactly as the scalar instruction with the same rounding mode.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 f2_pack(float a, float b) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(f32x2 v, float &a, float &b) {
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ f32x2 f2_mul_rn(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 f2_fma_rn(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ f32x2 f2_add_rn(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 f2_add_rz(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("add.rz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// int8 quantisation of two values by one scale, two lanes at a time:
+// c = sign(x) * floor(RN(|div_by(x, sc, rc)| + 0.5)), the code quant_code
+// gives for div_by(x, sc, rc) (RN is odd-symmetric, so |div_by(x)| =
+// div_by(|x|)).  floor(w) for 0 <= w < 2^23 is RZ(w + 2^23) - 2^23 (both
+// steps exact); re-signed and added to 1.5 * 2^23 it sits in the low
+// mantissa bits in two's complement, so the low byte of each result word is
+// the int8 code.  ress_check_scale_division compares it with the scalar
+// path over every fp16 x and amax.
+struct QuantScale {
+    f32x2 r, nd;  // (rc, rc), (-sc, -sc)
+};
+__device__ __forceinline__ QuantScale quant_scale(float sc, float rc) { return {f2_pack(rc, rc), f2_pack(-sc, -sc)}; }
+__device__ __forceinline__ void quant_code2(float x0, float x1, const QuantScale &s, uint32_t &c0, uint32_t &c1) {
+    const f32x2 a = f2_pack(fabsf(x0), fabsf(x1));
+    const f32x2 q = f2_mul_rn(a, s.r);
+    const f32x2 y = f2_fma_rn(f2_fma_rn(q, s.nd, a), s.r, q);
+    const f32x2 z = f2_add_rz(f2_add_rn(y, 0x3F0000003F000000ull), 0x4B0000004B000000ull);  // + 0.5, + 2^23
+    float f0, f1;
+    f2_unpack(f2_add_rn(z, 0xCB000000CB000000ull), f0, f1);  // - 2^23: floor as a float
+    const float g0 = __uint_as_float(__float_as_uint(f0) | (__float_as_uint(x0) & 0x80000000u));
+    const float g1 = __uint_as_float(__float_as_uint(f1) | (__float_as_uint(x1) & 0x80000000u));
+    float v0, v1;
+    f2_unpack(f2_add_rn(f2_pack(g0, g1), 0x4B4000004B400000ull), v0, v1);  // + 1.5 * 2^23
+    c0 = __float_as_uint(v0);
+    c1 = __float_as_uint(v1);
+}
+// Low bytes of four words, in order, as one word.
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3) {
+    return __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+}
+
 // Order-preserving uint32 key (fused_topm.py:51-56): -0 < +0.
 __device__ __forceinline__ uint32_t order_key(float x) {
     uint32_t u = __float_as_uint(x);

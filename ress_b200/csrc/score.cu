@@ -10,6 +10,8 @@
 //   SpargeAttn per_block_int8 (+ patch)     external/patches/spargeattn.patch:32-42
 // The operation order matches oracle/ress_oracle.c; see that file's header
 // for the numeric contract.
+#include <climits>
+
 #include "common.cuh"
 
 namespace ress {
@@ -404,6 +406,421 @@ __global__ void __launch_bounds__(POOL_NT) kquant_kernel(
     }
 }
 
+// ------------------------------------------------------- bf16 layer passes
+// Persistent forms of the three passes for bf16 layers (the common case):
+// each CTA walks tiles grid-stride and loads tile t + gridDim.x into
+// registers before working on tile t, so the HBM reads of the next tile
+// overlap this tile's arithmetic; the int8 codes come two per packed-fp32
+// instruction (quant_code2).  Same outputs, bit for bit, as the per-tile
+// kernels above (which serve fp32 layers).
+constexpr int PASS_BLOCKS_PER_SM = 4;
+
+__device__ __forceinline__ uint4 ldg16(const uint16_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t w_of(const uint4 &u, int j) { return j == 0 ? u.x : j == 1 ? u.y : j == 2 ? u.z : u.w; }
+// Full-layout token of the p-th patch / s-th special token (patch_tok /
+// special_tok with the frame index by invariant division).
+__device__ __forceinline__ long long patch_tok_f(int p, int S, int HW, const FastDiv &fhw) {
+    const int f = (int)fdiv((uint32_t)p, fhw);
+    return (long long)f * (HW + S) + S + (p - f * HW);
+}
+__device__ __forceinline__ long long special_tok_f(int s, int S, int HW, const FastDiv &fs) {
+    const int f = (int)fdiv((uint32_t)s, fs);
+    return (long long)f * (HW + S) + (s - f * S);
+}
+// max over |x| of the 8 bf16 values of u, as a bf16 pair (native bf16x2 max)
+__device__ __forceinline__ uint32_t absmax8(uint32_t acc, const uint4 &u) {
+    __nv_bfloat162 m = *reinterpret_cast<__nv_bfloat162 *>(&acc);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t a = w_of(u, j) & 0x7FFF7FFFu;
+        m = __hmax2(m, *reinterpret_cast<__nv_bfloat162 *>(&a));
+    }
+    return *reinterpret_cast<uint32_t *>(&m);
+}
+
+// Block-wide max of the per-thread amax, then the tile's scale RN(amax /
+// 127) and its correctly rounded reciprocal, computed once by warp 0 and
+// broadcast (every thread computing them was ~100 instructions each).
+struct TileScale {
+    float amax, sc, rc;
+};
+__device__ __forceinline__ TileScale block_tile_scale(float v, float *red) {
+    constexpr int NW = POOL_NT / 32;
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();  // earlier readers of red are done
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        float t = l < NW ? red[l] : 0.0f;
+        for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+        if (l == 0) {
+            const float sc = __fdiv_rn(t, 127.0f);
+            red[NW] = t;
+            red[NW + 1] = sc;
+            red[NW + 2] = sc != 0.0f ? __frcp_rn(sc) : 0.0f;
+        }
+    }
+    __syncthreads();
+    return {red[NW], red[NW + 1], red[NW + 2]};
+}
+
+// int8 codes of 8 values (4 pairs) as 8 bytes
+template <typename F>
+__device__ __forceinline__ uint2 quant8(F pair, const QuantScale &qs) {
+    uint32_t c[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float a, b;
+        pair(j, a, b);
+        quant_code2(a, b, qs, c[2 * j], c[2 * j + 1]);
+    }
+    return make_uint2(pack_low_bytes(c[0], c[1], c[2], c[3]), pack_low_bytes(c[4], c[5], c[6], c[7]));
+}
+
+// A Q tile whose |x| maximum lies outside [0.0157, 65520): fp16-round every
+// value first (as the per-tile generic kernel does); rare.
+__device__ __noinline__ void q_tile_outside(uint4 u0, uint4 u1, uint4 u2, uint4 u3, float amax_raw, int cnt,
+                                            int8_t *dst, float *scale_out) {
+    const float amax = f16r(amax_raw);  // fp16 rounding is monotone: max |f16r(x)| = f16r(max |x|)
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float rc = sc != 0.0f ? __frcp_rn(sc) : 0.0f;
+    if (threadIdx.x == 0) *scale_out = sc;
+    const uint4 u[4] = {u0, u1, u2, u3};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = threadIdx.x + k * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+        if (r >= cnt) continue;
+        uint32_t w[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t wv = w_of(u[k], j >> 1);
+            const float x = f16r(j & 1 ? bf_hi(wv) : bf_lo(wv));
+            const int qv = sc != 0.0f ? quant_code(div_by(x, sc, rc)) : 0;
+            w[j >> 2] |= ((uint32_t)(uint8_t)(int8_t)qv) << ((j & 3) * 8);
+        }
+        *reinterpret_cast<uint2 *>(dst + (size_t)r * 64 + c) = make_uint2(w[0], w[1]);
+    }
+}
+
+// Pass over Q (bf16), one 128-token tile per CTA: pooled Q and int8 Q.
+__global__ void __launch_bounds__(POOL_NT) pool_q_bf16_kernel(
+    const uint16_t *__restrict__ q, int H, int S, int HW, int Tp, long long sb, long long sh, long long st,
+    __nv_bfloat16 *__restrict__ qbar, int8_t *__restrict__ q8, float *__restrict__ qscale, FastDiv fhw) {
+    __shared__ __align__(16) uint16_t tb[KS_Q][72];
+    __shared__ float red[POOL_NT / 32 + 3];
+    const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z, nqb = gridDim.x;
+    const int bh = b * H + h;
+    const int t0 = qb * KS_Q, cnt = min(KS_Q, Tp - t0);
+    const uint16_t *base = q + b * sb + h * sh;
+    uint4 u[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = threadIdx.x + k * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+        u[k] = r < cnt ? ldg16(base + patch_tok_f(t0 + r, S, HW, fhw) * st + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    uint32_t m2 = 0u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = threadIdx.x + k * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+        if (qbar != nullptr) *reinterpret_cast<uint4 *>(&tb[r][c]) = u[k];
+        m2 = absmax8(m2, u[k]);
+    }
+    // syncs: tb complete
+    const TileScale ts = block_tile_scale(fmaxf(bf_lo(m2), bf_hi(m2)), red);
+    const float amax = ts.amax;
+    if (q8 != nullptr) {
+        int8_t *dst = q8 + ((size_t)bh * Tp + t0) * HD;
+        // In [0.0157, 65520) every bf16 x of fp16's normal range is exactly an fp16
+        // value, and every |x| < 2^-14 quantises to 0 with or without fp16 rounding
+        if (amax >= 0.0157f && amax < 65520.0f) {
+            const float sc = ts.sc;
+            const QuantScale qs = quant_scale(sc, ts.rc);
+            if (threadIdx.x == 0) qscale[(size_t)bh * nqb + qb] = sc;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = threadIdx.x + k * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+                if (r >= cnt) continue;
+                const uint4 uk = u[k];
+                *reinterpret_cast<uint2 *>(dst + (size_t)r * 64 + c) = quant8(
+                    [&](int j, float &a, float &bb) {
+                        const uint32_t w = w_of(uk, j);
+                        a = bf_lo(w);
+                        bb = bf_hi(w);
+                    },
+                    qs);
+            }
+        } else {
+            q_tile_outside(u[0], u[1], u[2], u[3], amax, cnt, dst, qscale + (size_t)bh * nqb + qb);
+        }
+    }
+    if (qbar != nullptr && threadIdx.x < HD / 2) {
+        // sequential window sums, two columns per thread
+        const int d = 2 * threadIdx.x;
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll 8
+        for (int r = 0; r < cnt; ++r) {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(&tb[r][d]);
+            s0 = __fadd_rn(s0, bf_lo(w));
+            s1 = __fadd_rn(s1, bf_hi(w));
+        }
+        const size_t o = ((size_t)bh * nqb + qb) * HD + d;
+        qbar[o] = __float2bfloat16_rn(__fdiv_rn(s0, (float)cnt));
+        qbar[o + 1] = __float2bfloat16_rn(__fdiv_rn(s1, (float)cnt));
+    }
+}
+
+// Pass over K or V (bf16), one 64-key tile per CTA.  K: pooled K and the
+// block sums of fp16(K) for the key mean; V: pooled V and fp16 V.  K and V
+// are separate passes so that the K quantisation, which runs right after
+// the K pass and the key mean, finds K still in L2.
+template <bool IS_K>
+__global__ void __launch_bounds__(POOL_NT) pool_kv1_bf16_kernel(
+    const uint16_t *__restrict__ x, int H, int S, int HW, int Tp, int Tk, long long sb, long long sh, long long st,
+    __nv_bfloat16 *__restrict__ xbar, uint16_t *__restrict__ v16, float *__restrict__ kpart, FastDiv fhw,
+    FastDiv fs) {
+    __shared__ __align__(16) uint16_t tb[KS_K][72];
+    const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z, nkb = gridDim.x;
+    const int bh = b * H + h;
+    const int nkp = (Tp + KS_K - 1) / KS_K;
+    const int c0 = kb * KS_K, nvalid = min(KS_K, Tk - c0);
+    const int npatch = max(0, min(KS_K, Tp - c0));
+    uint4 u[2];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        const int i = threadIdx.x + p * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+        const int cc = c0 + r;
+        const long long tok = cc < Tp ? patch_tok_f(cc, S, HW, fhw) : special_tok_f(cc - Tp, S, HW, fs);
+        u[p] = r < nvalid ? ldg16(x + b * sb + h * sh + c + tok * st) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        const int i = threadIdx.x + p * POOL_NT, r = i >> 3, c = (i & 7) * 8;
+        *reinterpret_cast<uint4 *>(&tb[r][c]) = u[p];
+        if (!IS_K && v16 != nullptr && r < nvalid) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t wv = w_of(u[p], j);
+                __half2 hv = __floats2half2_rn(bf_lo(wv), bf_hi(wv));
+                w[j] = *reinterpret_cast<uint32_t *>(&hv);
+            }
+            *reinterpret_cast<uint4 *>(v16 + ((size_t)bh * Tk + c0 + r) * HD + c) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    __syncthreads();
+    // sequential column sums, two columns per thread: warp 0 the pooled mean
+    // over the patch rows, warp 1 (K) fp16(K) over all rows
+    const int warp = threadIdx.x >> 5, d = 2 * (threadIdx.x & 31);
+    if (warp == 0 && xbar != nullptr && kb < nkp) {
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll 8
+        for (int r = 0; r < npatch; ++r) {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(&tb[r][d]);
+            s0 = __fadd_rn(s0, bf_lo(w));
+            s1 = __fadd_rn(s1, bf_hi(w));
+        }
+        __nv_bfloat16 *dst = xbar + ((size_t)bh * nkp + kb) * HD + d;
+        dst[0] = __float2bfloat16_rn(__fdiv_rn(s0, (float)npatch));
+        dst[1] = __float2bfloat16_rn(__fdiv_rn(s1, (float)npatch));
+    } else if (IS_K && warp == 1 && kpart != nullptr) {
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll 8
+        for (int r = 0; r < nvalid; ++r) {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(&tb[r][d]);
+            const float2 f = __half22float2(__floats2half2_rn(bf_lo(w), bf_hi(w)));
+            s0 = __fadd_rn(s0, f.x);
+            s1 = __fadd_rn(s1, f.y);
+        }
+        float *dst = kpart + ((size_t)bh * nkb + kb) * HD + d;
+        dst[0] = s0;
+        dst[1] = s1;
+    }
+}
+
+// Second pass over K (bf16): int8 of fp16(fp16(k) - km) per 64-key tile.
+// Persistent, KQ_NT threads with KQ_ROWS rows of 8 dims each; tile t +
+// gridDim.x is loaded into registers before tile t is quantised.
+// fp16(fp16(k) - km) is one fp16 subtraction: rounding the fp32 difference
+// of two fp16 values to fp16 equals rounding the exact difference once
+// (24 >= 2 * 11 + 2 significand bits), so __hsub2 gives the same bits.
+constexpr int KQ_NT = 128, KQ_ROWS = KS_K * 8 / KQ_NT, KQ_BLOCKS_PER_SM = 8;
+__device__ __forceinline__ TileScale block_tile_scale_kq(float v, float *red) {
+    constexpr int NW = KQ_NT / 32;
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        float t = l < NW ? red[l] : 0.0f;
+        for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+        if (l == 0) {
+            const float sc = __fdiv_rn(t, 127.0f);
+            red[NW] = t;
+            red[NW + 1] = sc;
+            red[NW + 2] = sc != 0.0f ? __frcp_rn(sc) : 0.0f;
+        }
+    }
+    __syncthreads();
+    return {red[NW], red[NW + 1], red[NW + 2]};
+}
+__global__ void __launch_bounds__(KQ_NT, KQ_BLOCKS_PER_SM) kquant_bf16_kernel(
+    const uint16_t *__restrict__ k, int H, int S, int HW, int Tp, int Tk, long long sb, long long sh, long long st,
+    const float *__restrict__ km, int8_t *__restrict__ k8, float *__restrict__ kscale, int nkb, int tiles,
+    FastDiv fnkb, FastDiv fh, FastDiv fhw, FastDiv fs) {
+    __shared__ float red[KQ_NT / 32 + 3];
+    const int c = (threadIdx.x & 7) * 8;  // this thread's 8 dims, the same for all of its rows
+    const int r0 = threadIdx.x >> 3;       // rows r0 + 16 p
+    auto load = [&](int t, uint4(&dst)[KQ_ROWS]) {
+        const int bh = (int)fdiv((uint32_t)t, fnkb), kb = t - bh * nkb;
+        const int b = (int)fdiv((uint32_t)bh, fh), h = bh - b * H;
+        const int c0 = kb * KS_K, nvalid = min(KS_K, Tk - c0);
+        const uint16_t *base = k + b * sb + h * sh + c;
+#pragma unroll
+        for (int p = 0; p < KQ_ROWS; ++p) {
+            const int r = r0 + p * (KQ_NT / 8), cc = c0 + r;
+            const long long tok = cc < Tp ? patch_tok_f(cc, S, HW, fhw) : special_tok_f(cc - Tp, S, HW, fs);
+            dst[p] = r < nvalid ? ldg16(base + tok * st) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    uint4 u[KQ_ROWS];
+    if ((int)blockIdx.x < tiles) load(blockIdx.x, u);
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        uint4 un[KQ_ROWS] = {};
+        const int tn = t + gridDim.x;
+        if (tn < tiles) load(tn, un);
+        const int bh = (int)fdiv((uint32_t)t, fnkb), kb = t - bh * nkb;
+        const int c0 = kb * KS_K, nvalid = min(KS_K, Tk - c0);
+        const float4 k0 = __ldg(reinterpret_cast<const float4 *>(km + (size_t)bh * HD + c));
+        const float4 k1 = __ldg(reinterpret_cast<const float4 *>(km + (size_t)bh * HD + c + 4));
+        const __half2 kmh[4] = {__floats2half2_rn(k0.x, k0.y), __floats2half2_rn(k0.z, k0.w),
+                                __floats2half2_rn(k1.x, k1.y), __floats2half2_rn(k1.z, k1.w)};
+        __half2 x[KQ_ROWS][4];
+        __half2 mx = __float2half2_rn(0.0f);
+        if (nvalid == KS_K) {
+#pragma unroll
+            for (int p = 0; p < KQ_ROWS; ++p)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t w = w_of(u[p], j);
+                    x[p][j] = __hsub2(__floats2half2_rn(bf_lo(w), bf_hi(w)), kmh[j]);
+                    mx = __hmax2(mx, __habs2(x[p][j]));
+                }
+        } else {
+#pragma unroll
+            for (int p = 0; p < KQ_ROWS; ++p) {
+                const bool valid = r0 + p * (KQ_NT / 8) < nvalid;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t w = w_of(u[p], j);
+                    x[p][j] = valid ? __hsub2(__floats2half2_rn(bf_lo(w), bf_hi(w)), kmh[j]) : __float2half2_rn(0.0f);
+                    mx = __hmax2(mx, __habs2(x[p][j]));
+                }
+            }
+        }
+        const float2 mf = __half22float2(mx);
+        const TileScale ts = block_tile_scale_kq(fmaxf(mf.x, mf.y), red);
+        const float sc = ts.sc, rc = ts.rc;
+        if (threadIdx.x == 0) kscale[(size_t)bh * nkb + kb] = sc;
+        int8_t *dst = k8 + ((size_t)bh * Tk + c0) * HD + c;
+        if (sc > 0.0f && sc < INFINITY) {
+            const QuantScale qs = quant_scale(sc, rc);
+#pragma unroll
+            for (int p = 0; p < KQ_ROWS; ++p) {
+                const int r = r0 + p * (KQ_NT / 8);
+                if (r >= nvalid) continue;
+                *reinterpret_cast<uint2 *>(dst + (size_t)r * 64) = quant8(
+                    [&](int j, float &a, float &bb) {
+                        const float2 f = __half22float2(x[p][j]);
+                        a = f.x;
+                        bb = f.y;
+                    },
+                    qs);
+            }
+        } else {
+#pragma unroll
+            for (int p = 0; p < KQ_ROWS; ++p) {
+                const int r = r0 + p * (KQ_NT / 8);
+                if (r >= nvalid) continue;
+                uint32_t w[2] = {0u, 0u};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float2 f = __half22float2(x[p][j >> 1]);
+                    const int qv = sc != 0.0f ? quant_code(div_by(j & 1 ? f.y : f.x, sc, rc)) : 0;
+                    w[j >> 2] |= ((uint32_t)(uint8_t)(int8_t)qv) << ((j & 3) * 8);
+                }
+                *reinterpret_cast<uint2 *>(dst + (size_t)r * 64) = make_uint2(w[0], w[1]);
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < KQ_ROWS; ++p) u[p] = un[p];
+    }
+}
+
+// km = fp16((sum over key blocks of the block sums) / Tk), sequential.
+// The block sums of one head go through shared memory in chunks of KM_ROWS:
+// all KM_NT threads fetch chunk c + 1 into registers while the first 64
+// threads add chunk c in order, so the loads are all in flight together.
+constexpr int KM_NT = 256, KM_ROWS = 128, KM_PER = KM_ROWS * HD / KM_NT / 4;  // float4 per thread per chunk
+__global__ void __launch_bounds__(KM_NT) key_mean_chunked_kernel(const float *__restrict__ kpart, int nkb, int Tk,
+                                                                 float *__restrict__ km) {
+    extern __shared__ float4 km_dyn[];  // two chunks of KM_ROWS x 64 floats
+    float *buf[2] = {reinterpret_cast<float *>(km_dyn), reinterpret_cast<float *>(km_dyn) + KM_ROWS * HD};
+    const int bh = blockIdx.x, tid = threadIdx.x;
+    const float4 *src = reinterpret_cast<const float4 *>(kpart + (size_t)bh * nkb * HD);
+    const int nch = (nkb + KM_ROWS - 1) / KM_ROWS;
+    const int n4 = nkb * HD / 4;  // float4 of this head
+    float4 r[KM_PER];
+#pragma unroll
+    for (int i = 0; i < KM_PER; ++i) {
+        const int e = tid + i * KM_NT;
+        r[i] = e < n4 ? __ldg(src + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < KM_PER; ++i) reinterpret_cast<float4 *>(buf[0])[tid + i * KM_NT] = r[i];
+    __syncthreads();
+    float s = 0.0f;
+    for (int c = 0; c < nch; ++c) {
+        if (c + 1 < nch) {
+#pragma unroll
+            for (int i = 0; i < KM_PER; ++i) {
+                const int e = (c + 1) * (KM_ROWS * HD / 4) + tid + i * KM_NT;
+                r[i] = e < n4 ? __ldg(src + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        if (tid < HD) {
+            const float *b = buf[c & 1] + tid;
+            const int rows = min(KM_ROWS, nkb - c * KM_ROWS);
+#pragma unroll 8
+            for (int j = 0; j < rows; ++j) s = __fadd_rn(s, b[j * HD]);
+        }
+        if (c + 1 < nch) {
+#pragma unroll
+            for (int i = 0; i < KM_PER; ++i) reinterpret_cast<float4 *>(buf[(c + 1) & 1])[tid + i * KM_NT] = r[i];
+        }
+        __syncthreads();
+    }
+    if (tid < HD) km[(size_t)bh * HD + tid] = f16r(__fdiv_rn(s, (float)Tk));
+}
+
+inline int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (dev >= 0 && dev < 64) cached[dev] = n;
+    return n;
+}
+inline int pass_grid(long long tiles) {
+    const long long cap = (long long)sm_count() * PASS_BLOCKS_PER_SM;
+    return (int)(tiles < cap ? tiles : cap);
+}
+
 // ------------------------------------------------------------------ predict
 constexpr int PRED_NT = 256;
 
@@ -575,8 +992,15 @@ template <typename T>
 static int pool_quant_q_t(const void *q, int B, int H, int frames, int S, int HW, long long sb, long long sh,
                           long long st, void *qbar, int8_t *q8, float *qscale, cudaStream_t s) {
     const int Tp = frames * HW, BH = B * H, nqb = (Tp + KS_Q - 1) / KS_Q;
-    pool_q_kernel<T><<<dim3(nqb, BH), POOL_NT, 0, s>>>((const T *)q, H, S, HW, Tp, sb, sh, st, (T *)qbar, q8,
-                                                      qscale);
+    if constexpr (sizeof(T) == 2) {
+        const long long tiles = (long long)nqb * BH;
+        if (tiles > INT_MAX) return RESS_E_SHAPE;
+        pool_q_bf16_kernel<<<dim3(nqb, H, B), POOL_NT, 0, s>>>((const uint16_t *)q, H, S, HW, Tp, sb, sh, st,
+                                                              (__nv_bfloat16 *)qbar, q8, qscale, make_fastdiv(HW));
+    } else {
+        pool_q_kernel<T><<<dim3(nqb, BH), POOL_NT, 0, s>>>((const T *)q, H, S, HW, Tp, sb, sh, st, (T *)qbar, q8,
+                                                          qscale);
+    }
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }
 
@@ -587,12 +1011,36 @@ static int pool_quant_kv_t(const void *k, const void *v, int B, int H, int frame
     const int Tp = frames * HW, Tk = Tp + frames * S, BH = B * H;
     const int nkb = (Tk + KS_K - 1) / KS_K;
     float *kpart = reinterpret_cast<float *>(ws);
-    pool_kv_kernel<T><<<dim3(nkb, BH), POOL_NT, 0, s>>>((const T *)k, (const T *)v, H, S, HW, Tp, Tk, sb, sh, st,
-                                                       (T *)kbar, (T *)vbar, v16, k8 ? kpart : nullptr);
-    if (k8 != nullptr) {
-        key_mean_kernel<<<BH, HD, 0, s>>>(kpart, nkb, Tk, km);
-        kquant_kernel<T><<<dim3(nkb, BH), POOL_NT, 0, s>>>((const T *)k, H, S, HW, Tp, Tk, sb, sh, st, km, k8,
-                                                          kscale);
+    if constexpr (sizeof(T) == 2) {
+        const long long tiles = (long long)nkb * BH;
+        if (tiles > INT_MAX) return RESS_E_SHAPE;
+        const FastDiv fhw = make_fastdiv(HW), fs = make_fastdiv(S > 0 ? S : 1);
+        const dim3 grid(nkb, H, B);
+        // K first, its quantisation right after (K still in L2), V last
+        if (kbar != nullptr || k8 != nullptr)
+            pool_kv1_bf16_kernel<true><<<grid, POOL_NT, 0, s>>>((const uint16_t *)k, H, S, HW, Tp, Tk, sb, sh, st,
+                                                                (__nv_bfloat16 *)kbar, nullptr, k8 ? kpart : nullptr,
+                                                                fhw, fs);
+        if (k8 != nullptr) {
+            const size_t km_smem = 2 * KM_ROWS * HD * sizeof(float);
+            set_smem_attr((const void *)key_mean_chunked_kernel, km_smem);
+            key_mean_chunked_kernel<<<BH, KM_NT, km_smem, s>>>(kpart, nkb, Tk, km);
+            const long long cap = (long long)sm_count() * KQ_BLOCKS_PER_SM;
+            kquant_bf16_kernel<<<(int)(tiles < cap ? tiles : cap), KQ_NT, 0, s>>>(
+                (const uint16_t *)k, H, S, HW, Tp, Tk, sb, sh, st, km, k8, kscale, nkb, (int)tiles,
+                make_fastdiv(nkb), make_fastdiv(H), fhw, fs);
+        }
+        if (vbar != nullptr || v16 != nullptr)
+            pool_kv1_bf16_kernel<false><<<grid, POOL_NT, 0, s>>>((const uint16_t *)v, H, S, HW, Tp, Tk, sb, sh, st,
+                                                                 (__nv_bfloat16 *)vbar, v16, nullptr, fhw, fs);
+    } else {
+        pool_kv_kernel<T><<<dim3(nkb, BH), POOL_NT, 0, s>>>((const T *)k, (const T *)v, H, S, HW, Tp, Tk, sb, sh,
+                                                           st, (T *)kbar, (T *)vbar, v16, k8 ? kpart : nullptr);
+        if (k8 != nullptr) {
+            key_mean_kernel<<<BH, HD, 0, s>>>(kpart, nkb, Tk, km);
+            kquant_kernel<T><<<dim3(nkb, BH), POOL_NT, 0, s>>>((const T *)k, H, S, HW, Tp, Tk, sb, sh, st, km, k8,
+                                                              kscale);
+        }
     }
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }
@@ -721,7 +1169,8 @@ extern "C" int ress_hess_adjust(const int32_t *base, const float *scores_norm, i
 namespace ress {
 // Every positive finite fp16 amax (blockIdx.x + 1 as fp16 bits) against every
 // fp16 x with |x| <= amax: the count of quotients where div_by differs from
-// IEEE division by the quantiser's scale RN(amax / 127).
+// IEEE division by the quantiser's scale RN(amax / 127), plus the count of
+// codes where the packed quantiser (quant_code2) differs from the scalar one.
 __global__ void check_division_kernel(int32_t *__restrict__ mismatches) {
     const uint16_t abits = (uint16_t)(blockIdx.x + 1);
     const float amax = __half2float(__ushort_as_half(abits));
@@ -733,6 +1182,11 @@ __global__ void check_division_kernel(int32_t *__restrict__ mismatches) {
         // compared as values: -0 and +0 quantise to the same code
         bad += (div_by(x, sc, rc) != __fdiv_rn(x, sc)) ? 1 : 0;
         bad += (div_by(-x, sc, rc) != __fdiv_rn(-x, sc)) ? 1 : 0;
+        // the packed two-lane quantiser against the scalar code
+        uint32_t c0, c1;
+        quant_code2(x, -x, quant_scale(sc, rc), c0, c1);
+        bad += ((int8_t)(c0 & 0xFFu) != (int8_t)quant_code(div_by(x, sc, rc))) ? 1 : 0;
+        bad += ((int8_t)(c1 & 0xFFu) != (int8_t)quant_code(div_by(-x, sc, rc))) ? 1 : 0;
     }
     if (bad) atomicAdd(mismatches, bad);
 }

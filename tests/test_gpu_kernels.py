@@ -66,6 +66,42 @@ def test_pooling_and_quant_bit_exact(shape, dtype):
     assert torch.equal(v16.cpu(), val.reshape(H, -1, 64).to(torch.float16))
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_pooling_and_quant_extreme_tiles(dtype):
+    """Tiles whose values are all tiny (|x| maximum below 0.0157: the fp16
+    rounding path), all zero, large (~1e4) or in fp16's subnormal range, in
+    runs of 300 tokens so that whole 128-query and 64-key tiles fall inside
+    one regime: the pooled means, int8 codes, scales and key mean stay
+    bit-identical to the oracle."""
+    shape = SMALL
+    q, k, v = synth.layer_qkv(shape, seed=3, dtype=torch.float32)
+    T = q.shape[-2]
+    runs = torch.tensor([1.0, 1e-3, 0.0, 3e3, 1e-6, 1.0, 2e-4])
+    f = runs[(torch.arange(T) // 300) % len(runs)].view(1, 1, T, 1)
+    q, k, v = ((x * f * g).to(dtype) for x, g in ((q, 1.0), (k, 0.7), (v, 1.3)))
+    L = _layout(shape)
+    qbar, q8, qs = K.pool_quant_q(q.cuda(), L)
+    kbar, vbar, k8, ks, v16, km = K.pool_quant_kv(k.cuda(), v.cuda(), L)
+    torch.cuda.synchronize()
+    qp, _ = synth.split_tokens(q, shape)
+    kp, ksp = synth.split_tokens(k, shape)
+    vp, vsp = synth.split_tokens(v, shape)
+    H = shape.n_heads
+    assert _eq(qbar, oracle.pool_mean(qp.reshape(H, -1, 64), 128))
+    assert _eq(kbar, oracle.pool_mean(kp.reshape(H, -1, 64), 64))
+    assert _eq(vbar, oracle.pool_mean(vp.reshape(H, -1, 64), 64))
+    key = torch.cat([kp, ksp], dim=-2)
+    val = torch.cat([vp, vsp], dim=-2)
+    q8o, qso, k8o, kso, kmo = oracle.quantize_qk(qp, key)
+    assert _eq(km, kmo)
+    assert torch.equal(q8.cpu(), q8o) and _eq(qs, qso)
+    assert torch.equal(k8.cpu(), k8o) and _eq(ks, kso)
+    assert torch.equal(v16.cpu(), val.reshape(H, -1, 64).to(torch.float16))
+    # the regimes were reached: zero, sub-window and large tiles among the Q scales
+    qsc = qs.cpu().flatten()
+    assert (qsc == 0).any() and ((qsc > 0) & (qsc < 0.0157 / 127)).any() and (qsc > 10).any()
+
+
 @pytest.mark.parametrize("shape,dtype", CASES)
 def test_predict_cond_baseline_bit_exact(shape, dtype):
     q, k, v = _inputs(shape, dtype)
