@@ -499,17 +499,23 @@ __global__ void __launch_bounds__(SEL_NT) map_lists_kernel(const uint8_t *__rest
 }
 
 // ----------------------------------------------------------------- restore-swap v2
-// The head's vbar stays resident in shared memory (bf16, 16-byte chunks of
-// row k stored at chunk position c ^ (k & 7), so a warp reading one row per
-// thread and 64 threads reading one column are both conflict-free) and one
-// CTA processes up to 8 q-block rows of that head, one 64-thread group (two
-// warps, named barrier 1 + g) per row.  Operation order is that of
+// The head's vbar stays resident in shared memory, transposed: column d
+// (one dimension over all pooled key blocks) is a contiguous bf16 row of
+// vbT with a row stride of 64m + 8 elements, so that
+//   - a drift chain (thread d walks its dimension over the candidates) reads
+//     eight candidates with one 16-byte load, the 64 threads' loads landing
+//     on distinct banks (rows 16 bytes apart modulo 128), and
+//   - a per-candidate pass (thread p takes four adjacent candidates, an FMA
+//     chain over the 64 dimensions each) reads the four with one 8-byte load.
+// One CTA processes up to 8 q-block rows of that head, one 64-thread group
+// (two warps, named barrier 1 + g) per row.  Operation order is that of
 // restore_swap_kernel / the oracle; only the placement of data changes.
+// (Measured before the transposition: the drift chains' per-element address
+// arithmetic and 2-byte loads were ~65 % of the kernel's instructions.)
 constexpr int G_NT = 64;
-
 // (d0, d1) = (a0 * b + c0, a1 * b + c1): two independent IEEE fp32 FMAs in one
 // issue slot (fma.rn.f32x2); each chain gets exactly the bits of __fmaf_rn.
-__device__ __forceinline__ void fma2_chain(float &c0, float &c1, float a0, float a1, float b) {
+__device__ __forceinline__ void fma2_chain_fwd(float &c0, float &c1, float a0, float a1, float b) {
     asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
         "mov.b64 ra, {%2, %3};\n\t"
         "mov.b64 rb, {%4, %4};\n\t"
@@ -519,6 +525,60 @@ __device__ __forceinline__ void fma2_chain(float &c0, float &c1, float a0, float
         : "+f"(c0), "+f"(c1)
         : "f"(a0), "f"(a1), "f"(b));
 }
+__host__ __device__ __forceinline__ int rs2_vstride(int nkp) { return ((nkp + 63) / 64) * 64 + 8; }
+__device__ __forceinline__ float bfl(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bfh(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Sequential fp32 FMA chain acc = sum_k w[k] * col[k] over k < n in k order
+// (w 16-byte aligned floats, col a vbT row), and (when want_sum) the
+// sequential fp32 sum of the weights.
+__device__ __forceinline__ float col_chain(const float *w, const uint16_t *col, int n, bool want_sum, float &sum) {
+    float acc = 0.0f, sp = 0.0f;
+    int k = 0;
+    for (; k + 8 <= n; k += 8) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(col + k);
+        const float4 p0 = *reinterpret_cast<const float4 *>(w + k);
+        const float4 p1 = *reinterpret_cast<const float4 *>(w + k + 4);
+        acc = __fmaf_rn(p0.x, bfl(v.x), acc);
+        acc = __fmaf_rn(p0.y, bfh(v.x), acc);
+        acc = __fmaf_rn(p0.z, bfl(v.y), acc);
+        acc = __fmaf_rn(p0.w, bfh(v.y), acc);
+        acc = __fmaf_rn(p1.x, bfl(v.z), acc);
+        acc = __fmaf_rn(p1.y, bfh(v.z), acc);
+        acc = __fmaf_rn(p1.z, bfl(v.w), acc);
+        acc = __fmaf_rn(p1.w, bfh(v.w), acc);
+        if (want_sum) {
+            sp = __fadd_rn(sp, p0.x);
+            sp = __fadd_rn(sp, p0.y);
+            sp = __fadd_rn(sp, p0.z);
+            sp = __fadd_rn(sp, p0.w);
+            sp = __fadd_rn(sp, p1.x);
+            sp = __fadd_rn(sp, p1.y);
+            sp = __fadd_rn(sp, p1.z);
+            sp = __fadd_rn(sp, p1.w);
+        }
+    }
+    for (; k < n; ++k) {
+        acc = __fmaf_rn(w[k], bf16_from_bits(col[k]), acc);
+        if (want_sum) sp = __fadd_rn(sp, w[k]);
+    }
+    sum = sp;
+    return acc;
+}
+
+// Four FMA chains over the 64 dimensions for candidates k0..k0+3 (k0 a
+// multiple of 4): a[i] = sum_d vbT[d][k0 + i] * b[d] in d order.
+__device__ __forceinline__ void quad_chains(const uint16_t *vbT, int vstride, int k0, const float *b, float (&a)[4]) {
+    a[0] = a[1] = a[2] = a[3] = 0.0f;
+#pragma unroll 16
+    for (int d = 0; d < HD; ++d) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(vbT + (size_t)d * vstride + k0);
+        const float bd = b[d];
+        fma2_chain_fwd(a[0], a[1], bfl(v.x), bfh(v.x), bd);
+        fma2_chain_fwd(a[2], a[3], bfl(v.y), bfh(v.y), bd);
+    }
+}
+
 
 __device__ __forceinline__ void gbar(int g) { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(G_NT) : "memory"); }
 
@@ -629,50 +689,17 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
     gbar(g);
 }
 
-__device__ __forceinline__ float vb_at(const uint16_t *vb, int k, int d) {
-    const int c = (d >> 3) ^ (k & 7);
-    return bf16_from_bits(vb[(size_t)k * HD + c * 8 + (d & 7)]);
-}
-__device__ __forceinline__ void vb_row(const uint16_t *vb, int k, float *v) {
-    const uint4 *row = reinterpret_cast<const uint4 *>(vb + (size_t)k * HD);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const uint4 u = row[c ^ (k & 7)];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            v[c * 8 + 2 * i] = __uint_as_float(w[i] << 16);
-            v[c * 8 + 2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-        }
-    }
-}
-
 // g, Mg, G, K, J of the current drop set, for one group.  The chains run
 // over every candidate with Pd[k] = drop[k] ? P[k] : +0: an accumulator that
 // starts at +0 is left bit-for-bit unchanged by adding a +0 or -0 product in
 // round-to-nearest, so this equals the sparse sum over the dropped entries
 // (the oracle's order) while letting the loads pipeline.
-__device__ void g_drift(GroupScratch &S, const float *P, float *Pd, const uint8_t *drop, const uint16_t *vb,
-                        const float *Mt, int n_cand, int g, int t) {
+__device__ void g_drift(GroupScratch &S, const float *P, float *Pd, const uint8_t *drop, const uint16_t *vbT,
+                        int vstride, const float *Mt, int n_cand, int g, int t) {
     for (int k = t; k < n_cand; k += G_NT) Pd[k] = drop[k] ? P[k] : 0.0f;
     gbar(g);
-    float acc = 0.0f, sp = 0.0f;
-    int k = 0;
-    for (; k + 8 <= n_cand; k += 8) {
-        float pv[8], vv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) { pv[u] = Pd[k + u]; vv[u] = vb_at(vb, k + u, t); }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc = __fmaf_rn(pv[u], vv[u], acc);
-        if (t == 0) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) sp = __fadd_rn(sp, pv[u]);
-        }
-    }
-    for (; k < n_cand; ++k) {
-        acc = __fmaf_rn(Pd[k], vb_at(vb, k, t), acc);
-        if (t == 0) sp = __fadd_rn(sp, Pd[k]);
-    }
+    float sp;
+    const float acc = col_chain(Pd, vbT + (size_t)t * vstride, n_cand, t == 0, sp);
     if (t == 0) S.sum_pd = bf16r(sp);
     gbar(g);
     const float gd = __fsub_rn(__fmul_rn(S.sum_pd, S.vq[t]), bf16r(acc));
@@ -705,16 +732,22 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     const int bh = blockIdx.x / ctas_per_head;
     const int q0 = (blockIdx.x % ctas_per_head) * rows_per_cta;
     const int h = bh % H;
-    uint16_t *vb = reinterpret_cast<uint16_t *>(dyn);
-    float *M = reinterpret_cast<float *>(dyn + (size_t)nkp * HD * 2);
+    const int vstride = rs2_vstride(nkp);
+    uint16_t *vbT = reinterpret_cast<uint16_t *>(dyn);
+    float *M = reinterpret_cast<float *>(dyn + (size_t)vstride * HD * 2);
     unsigned char *rows_base = reinterpret_cast<unsigned char *>(M + HD * HD);
-    // whole CTA: vbar (swizzled) and M
+    // whole CTA: vbar transposed, and M
     {
         const uint4 *src = reinterpret_cast<const uint4 *>(vb16 + (size_t)bh * nkp * HD);
-        uint4 *dst = reinterpret_cast<uint4 *>(vb);
         for (int i = threadIdx.x; i < nkp * 8; i += blockDim.x) {
             const int k = i >> 3, c = i & 7;
-            dst[k * 8 + (c ^ (k & 7))] = src[i];
+            const uint4 u = src[i];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                vbT[(size_t)(c * 8 + 2 * e) * vstride + k] = (uint16_t)(w[e] & 0xffffu);
+                vbT[(size_t)(c * 8 + 2 * e + 1) * vstride + k] = (uint16_t)(w[e] >> 16);
+            }
         }
         // M transposed: thread t then reads M[t][j] at Mt[j * HD + t], one bank per lane
         for (int i = threadIdx.x; i < HD * HD; i += blockDim.x) M[(i & (HD - 1)) * HD + (i >> 6)] = Mg_in[(size_t)h * HD * HD + i];
@@ -727,8 +760,8 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     unsigned char *rb = rows_base + (size_t)g * row_bytes;
     GroupScratch &S = *reinterpret_cast<GroupScratch *>(rb);
     float *P = reinterpret_cast<float *>(rb + ((sizeof(GroupScratch) + 15) & ~(size_t)15));
-    float *Pd = P + nkp;
-    float *ssq = Pd + n_cand;
+    float *Pd = P + ((nkp + 3) & ~3);  // 16-byte aligned: the chains read four weights at a time
+    float *ssq = Pd + ((n_cand + 3) & ~3);
     uint32_t *key = reinterpret_cast<uint32_t *>(ssq + n_cand);
     uint8_t *drop = reinterpret_cast<uint8_t *>(key + n_cand);
     uint8_t *best = drop + n_cand;
@@ -739,23 +772,8 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     for (int k = t; k < nkp; k += G_NT) P[k] = bf16r(DT<T>::load(attn, (size_t)row * nkp + k));
     gbar(g);
     {
-        float acc = 0.0f, s = 0.0f;
-        int k = 0;
-        for (; k + 8 <= nkp; k += 8) {
-            float pv[8], vv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) { pv[u] = P[k + u]; vv[u] = vb_at(vb, k + u, t); }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) acc = __fmaf_rn(pv[u], vv[u], acc);
-            if (t == 0) {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) s = __fadd_rn(s, pv[u]);
-            }
-        }
-        for (; k < nkp; ++k) {
-            acc = __fmaf_rn(P[k], vb_at(vb, k, t), acc);
-            if (t == 0) s = __fadd_rn(s, P[k]);
-        }
+        float s;
+        const float acc = col_chain(P, vbT + (size_t)t * vstride, nkp, t == 0, s);
         S.vq[t] = bf16r(acc);
         if (t == 0) S.tm = bf16r(s);
     }
@@ -787,27 +805,13 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
         key[k] = order_key(bf16r(__fdiv_rn(sv, den)));
         valid[k] = 1;
     };
-    {
-        // two candidates per step: two FMA chains in one packed instruction
-        int k = t;
-        for (; k + G_NT < n_cand; k += 2 * G_NT) {
-            float v0[HD], v1[HD];
-            vb_row(vb, k, v0);
-            vb_row(vb, k + G_NT, v1);
-            float a0 = 0.0f, a1 = 0.0f;
+    // four adjacent candidates per thread and step: four FMA chains, two per packed instruction
+    for (int k0 = 4 * t; k0 < n_cand; k0 += 4 * G_NT) {
+        float a[4];
+        quad_chains(vbT, vstride, k0, S.Mvq, a);
 #pragma unroll
-            for (int i = 0; i < HD; ++i) fma2_chain(a0, a1, v0[i], v1[i], S.Mvq[i]);
-            cut(k, a0);
-            cut(k + G_NT, a1);
-        }
-        if (k < n_cand) {
-            float v0[HD];
-            vb_row(vb, k, v0);
-            float a0 = 0.0f;
-#pragma unroll
-            for (int i = 0; i < HD; ++i) a0 = __fmaf_rn(S.Mvq[i], v0[i], a0);
-            cut(k, a0);
-        }
+        for (int i = 0; i < 4; ++i)
+            if (k0 + i < n_cand) cut(k0 + i, a[i]);
     }
     gbar(g);
     const int nt = nts[row];
@@ -815,14 +819,14 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     for (int k = t; k < n_cand; k += G_NT) drop[k] = sel[k] ? 0 : 1;
     gbar(g);
     if (track_best) {
-        g_drift(S, P, Pd, drop, vb, M, n_cand, g, t);
+        g_drift(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
         if (t == 0) S.bestJ = S.J;
         for (int k = t; k < n_cand; k += G_NT) best[k] = drop[k];
         gbar(g);
     }
     for (int it = 0; it < n_iters; ++it) {
         const int pic = (int)rintf(__fmul_rn(fr.f[it], (float)nt));
-        g_drift(S, P, Pd, drop, vb, M, n_cand, g, t);
+        g_drift(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
         if (t == 0) {
             S.flag = (track_best && S.J < S.bestJ) ? 1 : 0;
             if (S.flag) S.bestJ = S.J;
@@ -850,25 +854,12 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
             }
             valid[k] = drop[k] ? 0 : 1;
         };
-        // two candidates per step: two independent FMA chains in flight
-        int k = t;
-        for (; k + G_NT < n_cand; k += 2 * G_NT) {
-            float v0[HD], v1[HD];
-            vb_row(vb, k, v0);
-            vb_row(vb, k + G_NT, v1);
-            float a0 = 0.0f, a1 = 0.0f;
+        for (int k0 = 4 * t; k0 < n_cand; k0 += 4 * G_NT) {
+            float a[4];
+            quad_chains(vbT, vstride, k0, S.Mgb, a);
 #pragma unroll
-            for (int j = 0; j < HD; ++j) fma2_chain(a0, a1, v0[j], v1[j], S.Mgb[j]);
-            quality(k, a0);
-            quality(k + G_NT, a1);
-        }
-        if (k < n_cand) {
-            float v0[HD];
-            vb_row(vb, k, v0);
-            float a0 = 0.0f;
-#pragma unroll
-            for (int j = 0; j < HD; ++j) a0 = __fmaf_rn(v0[j], S.Mgb[j], a0);
-            quality(k, a0);
+            for (int i = 0; i < 4; ++i)
+                if (k0 + i < n_cand) quality(k0 + i, a[i]);
         }
         const int n_drop = gsum(nd, S.red, g, t);
         const int n_kept = gsum(nk, S.red, g, t);
@@ -884,7 +875,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
         gbar(g);
     }
     if (track_best) {
-        g_drift(S, P, Pd, drop, vb, M, n_cand, g, t);
+        g_drift(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
         if (!(S.J < S.bestJ))
             for (int k = t; k < n_cand; k += G_NT) drop[k] = best[k];
         gbar(g);
@@ -918,9 +909,11 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
 }
 
 static size_t rs2_row_bytes(int nkp, int n_cand) {
-    size_t b = ((sizeof(GroupScratch) + 15) & ~(size_t)15) + (size_t)nkp * 4 + (size_t)n_cand * (4 + 4 + 4 + 5);
+    size_t b = ((sizeof(GroupScratch) + 15) & ~(size_t)15) + (size_t)((nkp + 3) & ~3) * 4 +
+               (size_t)((n_cand + 3) & ~3) * 4 + (size_t)n_cand * (4 + 4 + 5);
     return (b + 15) & ~(size_t)15;
 }
+static size_t rs2_fixed_bytes(int nkp) { return (size_t)rs2_vstride(nkp) * HD * 2 + (size_t)HD * HD * 4; }
 
 static size_t rs_smem(int nkp, int n_cand) {
     return (size_t)STAGE_BYTES + (size_t)((nkp + 7) & ~7) * 2 + (size_t)((n_cand + 7) & ~7) * 2 +
@@ -943,7 +936,7 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
     for (int i = 0; i < MAX_ITERS; ++i) fr.f[i] = i < n_iters ? fracs[i] : 0.0f;
     {
         // v2: vbar resident in shared memory, up to 8 rows per CTA
-        const size_t fixed = (size_t)nkp * HD * 2 + (size_t)HD * HD * 4;
+        const size_t fixed = rs2_fixed_bytes(nkp);
         const size_t rowb = rs2_row_bytes(nkp, n_cand);
         int R = 8;
         while (R > 0 && fixed + (size_t)R * rowb > 220 * 1024) --R;
@@ -1006,7 +999,7 @@ extern "C" int ress_restore_swap(int dtype, const void *attn_full, const void *v
         return RESS_E_ARG;
     if (counts && (!status || list_width <= 0)) return RESS_E_ARG;
     if (lists && !counts) return RESS_E_ARG;
-    if (rs_smem(nkp, n_cand) > 200 * 1024 && (size_t)nkp * HD * 2 + HD * HD * 4 + 2 * rs2_row_bytes(nkp, n_cand) > 220 * 1024)
+    if (rs_smem(nkp, n_cand) > 200 * 1024 && rs2_fixed_bytes(nkp) + 2 * rs2_row_bytes(nkp, n_cand) > 220 * 1024)
         return RESS_E_SHAPE;
     cudaStream_t st = (cudaStream_t)stream;
     if (dtype == RESS_F32)
