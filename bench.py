@@ -51,6 +51,8 @@ def _args():
     ap.add_argument("--frames", type=int, default=N_FRAMES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-attn", action="store_true", help="one small layer, for ncu")
+    ap.add_argument("--profile-rs", action="store_true",
+                    help="restore-swap on the cfg2 layer with 0/1/5 rounds and track-best off/on, for ncu")
     ap.add_argument("--eager", action="store_true", help="time eager calls instead of CUDA-graph replays")
     ap.add_argument("--shard", default="heads", choices=["heads", "views"],
                     help="views: frames split over the ranks, K/V all-gathered (whole-model sharding)")
@@ -680,6 +682,38 @@ def profile_attn():
     torch.cuda.synchronize()
 
 
+def profile_rs():
+    """Restore-swap phase split for ncu: the cfg2 layer's restore-swap run as
+    (rounds, track-best) = (0, off), (0, on), (5, on), (1, off), one launch
+    each after a warm-up pass, with CUDA-event times printed."""
+    from ress_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    S = _setup(N_FRAMES, 1, 0, dev)
+    L = S["L"]
+    qbar, _, _ = K.pool_quant_q(S["q"], L)
+    kbar, vbar, _, _, _, _ = K.pool_quant_kv(S["k"], S["v"], L)
+    af, ac = K.predict(qbar, kbar, L.n_cand)
+    base = K.baseline(ac, SPARSE_RATIO).view(1, L.H, L.nq)
+    nts = K.hess_adjust(base, S["budget"].scores_norm, L.n_cand, min_clamp=2).view(-1)
+    M = S["order"].M
+    runs = [(0, False), (0, True), (5, True), (1, False)]
+
+    def rs(n, tb):
+        K.restore_swap(af, vbar, M, nts, L.n_cand, n_iters=n, track_best=tb, sink_blocks=L.sink_blocks)
+
+    for n, tb in runs:
+        rs(n, tb)
+    torch.cuda.synchronize()
+    for n, tb in runs:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record()
+        rs(n, tb)
+        ev[1].record()
+        ev[1].synchronize()
+        print(f"restore_swap rounds={n} track_best={int(tb)}: {ev[0].elapsed_time(ev[1]):.4f} ms", flush=True)
+
+
 def main():
     args = _args()
     global SPARSE_RATIO
@@ -687,6 +721,9 @@ def main():
         SPARSE_RATIO = args.sparse_ratio
     if args.profile_attn:
         profile_attn()
+        return
+    if args.profile_rs:
+        profile_rs()
         return
     if args.sweep:
         run_sweep(args)
