@@ -51,6 +51,8 @@ def _args():
     ap.add_argument("--frames", type=int, default=N_FRAMES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-attn", action="store_true", help="one small layer, for ncu")
+    ap.add_argument("--profile-score", action="store_true",
+                    help="the scoring passes (pooling, quantisation, key mean) on the cfg2 layer, for ncu")
     ap.add_argument("--profile-rs", action="store_true",
                     help="restore-swap on the cfg2 layer with 0/1/5 rounds and track-best off/on, for ncu")
     ap.add_argument("--eager", action="store_true", help="time eager calls instead of CUDA-graph replays")
@@ -333,10 +335,14 @@ def run_ress(args):
     mixed_peak = 2.0 / (1.0 / bf16_peak + 1.0 / (2.0 * bf16_peak))
     achieved = attn_flops / (attn_ms / 1000.0) / 1e12
 
-    # stage breakdown (eager calls, the second of two instrumented steps)
+    # stage breakdown (eager calls, the second of two instrumented steps).  A
+    # device-side sleep is queued first so that the host has enqueued the
+    # whole step before it starts: the events then bracket device time only,
+    # not the gaps of eager launches.
     stages = {}
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
     for _ in range(2):
+        torch.cuda._sleep(40_000_000)
         ev[0].record(stream)
         qbar, q8, qs = K.pool_quant_q(S["q"], L)
         kbar, vbar, k8, ks, v16, km = K.pool_quant_kv(S["k"], S["v"], L)
@@ -682,6 +688,39 @@ def profile_attn():
     torch.cuda.synchronize()
 
 
+def profile_score():
+    """Scoring passes for ncu: the cfg2 layer's Q pass and K/V passes (pooled
+    means, int8 Q and K, fp16 V, key mean), three times each; CUDA-event
+    times of the third printed."""
+    from ress_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    S = _setup(N_FRAMES, 1, 0, dev)
+    L = S["L"]
+    ws = K.workspace(dev, L.B * L.H, L.Tp, L.Tk, L.n_cand)
+    for i in range(3):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        torch.cuda._sleep(20_000_000)
+        ev[0].record()
+        K.pool_quant_q(S["q"], L)
+        ev[1].record()
+        K.pool_quant_kv(S["k"], S["v"], L, ws=ws)
+        ev[2].record()
+        ev[2].synchronize()
+    q_ms, kv_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    mb = 1e6
+    print(f"Q pass {q_ms * 1e3:.1f} us, K/V passes {kv_ms * 1e3:.1f} us; algorithmic bytes "
+          f"(Q, K, V read once + int8 Q, K written) {SCORE_BYTES(L) / mb:.0f} MB -> "
+          f"{SCORE_BYTES(L) / ((q_ms + kv_ms) * 1e-3) / 1e9:.0f} GB/s", flush=True)
+
+
+def SCORE_BYTES(L):
+    """Algorithmic bytes of the scoring passes: Q, K, V (bf16) read once and
+    int8 Q and K written (pooled means and scales are < 2 %)."""
+    n = L.B * L.H * 64
+    return n * (L.Tp * 2 + L.Tk * 2 * 2) + n * (L.Tp + L.Tk)
+
+
 def profile_rs():
     """Restore-swap phase split for ncu: the cfg2 layer's restore-swap run as
     (rounds, track-best) = (0, off), (0, on), (5, on), (1, off), one launch
@@ -724,6 +763,9 @@ def main():
         return
     if args.profile_rs:
         profile_rs()
+        return
+    if args.profile_score:
+        profile_score()
         return
     if args.sweep:
         run_sweep(args)
