@@ -721,14 +721,15 @@ def SCORE_BYTES(L):
     return n * (L.Tp * 2 + L.Tk * 2 * 2) + n * (L.Tp + L.Tk)
 
 
-def profile_rs():
-    """Restore-swap phase split for ncu: the cfg2 layer's restore-swap run as
-    (rounds, track-best) = (0, off), (0, on), (5, on), (1, off), one launch
-    each after a warm-up pass, with CUDA-event times printed."""
+def profile_rs(frames=N_FRAMES):
+    """Restore-swap phase split for ncu: the layer's restore-swap (cfg2 by
+    default, --frames for others) run as (rounds, track-best) = (0, off),
+    (0, on), (5, on), (1, off), one launch each after a warm-up pass, with
+    CUDA-event times printed."""
     from ress_b200 import kernels as K
 
     dev = torch.device("cuda", 0)
-    S = _setup(N_FRAMES, 1, 0, dev)
+    S = _setup(frames, 1, 0, dev)
     L = S["L"]
     qbar, _, _ = K.pool_quant_q(S["q"], L)
     kbar, vbar, _, _, _, _ = K.pool_quant_kv(S["k"], S["v"], L)
@@ -762,7 +763,7 @@ def main():
         profile_attn()
         return
     if args.profile_rs:
-        profile_rs()
+        profile_rs(args.frames)
         return
     if args.profile_score:
         profile_score()

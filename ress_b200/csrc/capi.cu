@@ -22,7 +22,8 @@ extern "C" size_t ress_workspace_size(int BH, int Tp, int Tk, int n_cand) {
     const size_t nkb = (size_t)(Tk + 63) / 64, nkp = (size_t)(Tp + 63) / 64;
     // ress_score_quant: per-key-block fp32 sums for the key mean
     const size_t quant = (size_t)BH * nkb * 64 * sizeof(float);
-    // ress_restore_swap: bf16 copy of vbar + per-candidate term_k
-    const size_t rs = (((size_t)BH * nkp * 64 * 2 + 255) & ~(size_t)255) + (size_t)BH * n_cand * sizeof(float);
+    // ress_restore_swap: bf16 copy of vbar + per-candidate term_k (+ the
+    // transposed copy for layers too large for shared memory)
+    const size_t rs = ress::rs_scratch_bytes(BH, (int)nkp, n_cand);
     return (quant > rs ? quant : rs) + 256;
 }

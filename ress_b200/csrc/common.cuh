@@ -114,6 +114,9 @@ __device__ __forceinline__ float div_by(float x, float d, float r) {
     return __fmaf_rn(rem, r, q);
 }
 
+// Workspace bytes ress_restore_swap needs (select.cu).
+size_t rs_scratch_bytes(int BH, int nkp, int n_cand);
+
 // -------------------------------------------------------- invariant division
 // n / d for a divisor fixed per launch, by multiply-high (T. Granlund and
 // P. Montgomery, "Division by invariant integers using multiplication",

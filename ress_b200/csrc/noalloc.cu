@@ -34,12 +34,10 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void *g_scratch_addr[kMaxDevices] = {nullptr};
 
-// Same layout ress_restore_swap uses inside its workspace: the bf16 copy of
-// vbar at offset 0, then (256-byte aligned) one fp32 term per candidate.
-size_t restore_swap_scratch_bytes(int BH, int nkp, int n_cand) {
-    const size_t vb = ((size_t)BH * nkp * 64 * 2 + 255) & ~(size_t)255;
-    return vb + (size_t)BH * n_cand * sizeof(float);
-}
+// The workspace ress_restore_swap uses: the bf16 copy of vbar, one fp32 term
+// per candidate and, for layers too large for shared memory, the transposed
+// copy of vbar.
+size_t restore_swap_scratch_bytes(int BH, int nkp, int n_cand) { return ress::rs_scratch_bytes(BH, nkp, n_cand); }
 
 }  // namespace
 

@@ -61,11 +61,13 @@ __device__ void emit_list(const uint8_t *keep, int n_cand, int lead, int sink_bl
 
 // ----------------------------------------------------------------- vbar terms
 // Per head: bf16 copy of vbar and quadratic_deviation's term_k =
-// bf16(sum_i bf16(Mvk_i * v_i)), Mvk = bf16(M_bf16 v) (projected.py:283-285).
+// bf16(sum_i bf16(Mvk_i * v_i)), Mvk = bf16(M_bf16 v) (projected.py:283-285);
+// for the streamed restore-swap kernel also the transposed bf16 copy
+// vbT[bh][d][k] (row stride vt_stride).
 template <typename T>
 __global__ void vbar_terms_kernel(const T *__restrict__ vbar, const float *__restrict__ M, int H,
                                   int nkp, int n_cand, uint16_t *__restrict__ vb16,
-                                  float *__restrict__ tk) {
+                                  float *__restrict__ tk, uint16_t *__restrict__ vbT, int vt_stride) {
     __shared__ float Mb[HD * HD];
     const int bh = blockIdx.y, h = bh % H;
     for (int i = threadIdx.x; i < HD * HD; i += blockDim.x) Mb[i] = bf16r(M[(size_t)h * HD * HD + i]);
@@ -77,6 +79,7 @@ __global__ void vbar_terms_kernel(const T *__restrict__ vbar, const float *__res
     for (int j = 0; j < HD; ++j) {
         v[j] = bf16r(DT<T>::load(vbar, ((size_t)bh * nkp + k) * HD + j));
         vb16[((size_t)bh * nkp + k) * HD + j] = bf16bits(v[j]);
+        if (vbT != nullptr) vbT[((size_t)bh * HD + j) * vt_stride + k] = bf16bits(v[j]);
     }
     if (k >= n_cand) return;
     float s = 0.0f;
@@ -112,13 +115,22 @@ __device__ __forceinline__ void load_row64(const uint16_t *src, float *v) {
     }
 }
 
-// Rows of vbar per shared-memory stage of the drift chains: DSTAGES stages
-// in a ring, filled with cp.async DSTAGES - 1 chunks ahead of the chain (the
-// lead covers the L2 latency; measured: one 64-row chunk ahead left the
-// chain waiting on every chunk).
-constexpr int DCH = 32;
-constexpr int DSTAGES = 8;
-constexpr int STAGE_BYTES = DSTAGES * DCH * HD * 2;
+// Candidates per shared-memory stage of the drift chains: DSTAGES stages in
+// a ring, filled with cp.async DSTAGES - 1 chunks ahead of the chain (the
+// lead covers the L2 latency; measured: one chunk ahead left the chain
+// waiting on every chunk).  A stage holds the chunk transposed, [64 dims]
+// x [DCH candidates] with a row stride of DCH + 8 (rows 16 bytes apart
+// modulo 128, so the 64 chain threads' 16-byte reads are conflict-free):
+// a chain thread reads eight candidates of its dimension per load.
+// (Measured before the transposition, with row-major 32-row stages: ~30
+// clk per candidate per chain, the 2-byte column loads and their address
+// arithmetic plus two CTA barriers per 32 candidates.)
+constexpr int DCH = 64;
+constexpr int DSTAGES = 4;
+constexpr int STAGE_ROW = DCH + 8;
+constexpr int STAGE_BYTES = DSTAGES * HD * STAGE_ROW * 2;
+__device__ __forceinline__ float rs_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float rs_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
@@ -132,22 +144,27 @@ __device__ __forceinline__ void cp_async_wait_lead() {
 // acc[d] = sum_k w(k) * vbar[k][d] for d = tid < 64 as one sequential fp32
 // FMA chain per dimension in k order (with w(k) = +0 for masked entries,
 // which leaves the chain bit-for-bit unchanged: it starts at +0 and never
-// reaches -0), and total = sequential fp32 sum of w(k) (thread 64).  vbar
-// rows stream through a ring of shared-memory stages of DCH rows loaded by
-// the whole CTA with cp.async.  MASKED: w(k) = mask[k] ? P[k] : +0, else
+// reaches -0), and total = sequential fp32 sum of w(k) (thread 64).  The
+// transposed vbar (vbt: this head's [64][vt_stride] bf16) streams through a
+// ring of shared-memory stages of DCH candidates loaded by the whole CTA
+// with cp.async.  MASKED: w(k) = mask[k] ? P[k] : +0, else
 // P[k].  P (bf16 bits) is 16-byte aligned and mask 8-byte aligned: eight
 // weights come in one 16-byte and one 8-byte load, so the loads of a batch
 // overlap instead of each waiting on the mask byte before it.
 template <bool MASKED>
-__device__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t *vb, int n, uint16_t *stage,
-                         float &acc_out, float &total_out) {
+__device__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t *vbt, int vt_stride, int n,
+                         uint16_t *stage, float &acc_out, float &total_out) {
     const int tid = threadIdx.x;
     const int nch = (n + DCH - 1) / DCH;
     auto issue = [&](int c) {
-        const int r0 = c * DCH, rows = min(DCH, n - r0);
-        uint16_t *dst = stage + (c % DSTAGES) * DCH * HD;
-        for (int i = tid; i < rows * 8; i += SEL_NT)
-            cp_async16(dst + i * 8, vb + (size_t)r0 * HD + (size_t)i * 8);
+        // 16-byte pieces (8 candidates of one dimension); the last chunk's
+        // final piece may run past n but stays inside the padded vbt row
+        const int k0 = c * DCH, pieces = (min(DCH, n - k0) + 7) / 8;
+        uint16_t *dst = stage + (c % DSTAGES) * HD * STAGE_ROW;
+        for (int i = tid; i < HD * (DCH / 8); i += SEL_NT) {
+            const int d = i / (DCH / 8), q = i % (DCH / 8);
+            if (q < pieces) cp_async16(dst + d * STAGE_ROW + q * 8, vbt + (size_t)d * vt_stride + k0 + q * 8);
+        }
     };
     auto weights8 = [&](int k0, float (&w)[8]) {
         const uint4 pw = *reinterpret_cast<const uint4 *>(P + k0);
@@ -180,18 +197,24 @@ __device__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t 
         cp_async_wait_lead();  // chunk c has landed (this thread's copies)
         __syncthreads();       // ... and every thread's
         const int r0 = c * DCH, rows = min(DCH, n - r0);
-        const uint16_t *st = stage + (c % DSTAGES) * DCH * HD;
+        const uint16_t *st = stage + (c % DSTAGES) * HD * STAGE_ROW;
         if (tid < HD) {
+            const uint16_t *col = st + tid * STAGE_ROW;
             int r = 0;
             for (; r + 8 <= rows; r += 8) {
-                float w[8], v[8];
+                float w[8];
                 weights8(r0 + r, w);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = bf16_from_bits(st[(r + u) * HD + tid]);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) acc = __fmaf_rn(w[u], v[u], acc);
+                const uint4 v = *reinterpret_cast<const uint4 *>(col + r);
+                acc = __fmaf_rn(w[0], rs_lo(v.x), acc);
+                acc = __fmaf_rn(w[1], rs_hi(v.x), acc);
+                acc = __fmaf_rn(w[2], rs_lo(v.y), acc);
+                acc = __fmaf_rn(w[3], rs_hi(v.y), acc);
+                acc = __fmaf_rn(w[4], rs_lo(v.z), acc);
+                acc = __fmaf_rn(w[5], rs_hi(v.z), acc);
+                acc = __fmaf_rn(w[6], rs_lo(v.w), acc);
+                acc = __fmaf_rn(w[7], rs_hi(v.w), acc);
             }
-            for (; r < rows; ++r) acc = __fmaf_rn(weight1(r0 + r), bf16_from_bits(st[r * HD + tid]), acc);
+            for (; r < rows; ++r) acc = __fmaf_rn(weight1(r0 + r), bf16_from_bits(col[r]), acc);
         } else if (tid == HD) {
             int r = 0;
             for (; r + 8 <= rows; r += 8) {
@@ -210,11 +233,11 @@ __device__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t 
 
 // g, Mg, G = ||g||^2_M and K for the current drop set (projected.py:868-878,
 // 908-920).  vb: bf16 bits (nkp, 64) of this head.  S.Mt holds M transposed.
-__device__ void rs_drift(RSShared &S, const uint16_t *P, const uint8_t *drop, const uint16_t *vb,
+__device__ void rs_drift(RSShared &S, const uint16_t *P, const uint8_t *drop, const uint16_t *vbt, int vt_stride,
                          int n_cand, uint16_t *stage) {
     const int tid = threadIdx.x;
     float acc, tot;
-    rs_chain<true>(P, drop, vb, n_cand, stage, acc, tot);
+    rs_chain<true>(P, drop, vbt, vt_stride, n_cand, stage, acc, tot);
     if (tid < HD) S.g[tid] = bf16r(acc);  // masked_vbar_d, finished below
     else if (tid == HD) S.sum_pd = bf16r(tot);
     __syncthreads();
@@ -243,7 +266,8 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     const float *__restrict__ M, const int32_t *__restrict__ nts, int H, int nq, int nkp, int n_cand,
     int n_iters, Fracs fr, int track_best, uint8_t *__restrict__ drop_out,
     uint16_t *__restrict__ s_out, int32_t *__restrict__ lists, int32_t *__restrict__ counts,
-    int list_width, int sink_blocks, int lead, int32_t *__restrict__ status) {
+    int list_width, int sink_blocks, int lead, int32_t *__restrict__ status, const uint16_t *__restrict__ vbT,
+    int vt_stride) {
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ RSShared S;
     const int row = blockIdx.x;
@@ -261,6 +285,7 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     uint8_t *sel = valid + n_cand;
     uint8_t *sel2 = sel + n_cand;
     const uint16_t *vb = vb16 + (size_t)bh * nkp * HD;
+    const uint16_t *vbt = vbT + (size_t)bh * HD * vt_stride;
 
     for (int i = tid; i < HD * HD; i += SEL_NT) S.Mt[(i & (HD - 1)) * HD + (i >> 6)] = M[(size_t)h * HD * HD + i];
     for (int k = tid; k < nkp; k += SEL_NT) P[k] = bf16bits(DT<T>::load(attn, (size_t)row * nkp + k));
@@ -268,7 +293,7 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     // dense_reference over all pooled blocks: v_bar_query = P @ v_bar, total = sum(P)
     {
         float acc, tot;
-        rs_chain<false>(P, nullptr, vb, nkp, stage, acc, tot);
+        rs_chain<false>(P, nullptr, vbt, vt_stride, nkp, stage, acc, tot);
         if (tid < HD) S.vq[tid] = bf16r(acc);
         else if (tid == HD) S.tm = bf16r(tot);
     }
@@ -314,14 +339,14 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     for (int k = tid; k < n_cand; k += SEL_NT) drop[k] = sel[k] ? 0 : 1;
     __syncthreads();
     if (track_best) {
-        rs_drift(S, P, drop, vb, n_cand, stage);
+        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage);
         if (tid == 0) S.bestJ = S.J;
         for (int k = tid; k < n_cand; k += SEL_NT) best[k] = drop[k];
         __syncthreads();
     }
     for (int it = 0; it < n_iters; ++it) {
         const int pic = (int)rintf(__fmul_rn(fr.f[it], (float)nt));
-        rs_drift(S, P, drop, vb, n_cand, stage);
+        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage);
         if (tid == 0) {
             S.flag = (track_best && S.J < S.bestJ) ? 1 : 0;
             if (S.flag) S.bestJ = S.J;
@@ -370,7 +395,7 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
         __syncthreads();
     }
     if (track_best) {
-        rs_drift(S, P, drop, vb, n_cand, stage);
+        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage);
         const bool keep_final = S.J < S.bestJ;
         if (!keep_final)
             for (int k = tid; k < n_cand; k += SEL_NT) drop[k] = best[k];
@@ -920,6 +945,22 @@ static size_t rs_smem(int nkp, int n_cand) {
            (size_t)((n_cand + 3) & ~3) * 4 + (size_t)n_cand * 5;
 }
 
+// The streamed kernel is used when the v2 kernel cannot hold the head's
+// pooled values plus two rows in shared memory.
+static bool rs_uses_v2(int nkp, int n_cand) {
+    return rs2_fixed_bytes(nkp) + 2 * rs2_row_bytes(nkp, n_cand) <= 220 * 1024;
+}
+static int rs_vt_stride(int nkp) { return (nkp + 7) & ~7; }
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+// Workspace of ress_restore_swap: bf16 vbar (BH, nkp, 64), then fp32 term_k
+// (BH, n_cand), then -- streamed kernel only -- the transposed bf16 vbar
+// (BH, 64, vt_stride); each part 256-byte aligned.
+size_t rs_scratch_bytes(int BH, int nkp, int n_cand) {
+    size_t b = align256((size_t)BH * nkp * HD * 2) + (size_t)BH * n_cand * sizeof(float);
+    if (!rs_uses_v2(nkp, n_cand)) b = align256(b) + (size_t)BH * HD * rs_vt_stride(nkp) * 2;
+    return b;
+}
+
 template <typename T>
 static int restore_swap_t(const void *attn_full, const void *vbar, const float *M, const int32_t *nts,
                           int B, int H, int nq, int nkp, int n_cand, int n_iters, const float *fracs,
@@ -928,10 +969,15 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
                           cudaStream_t st) {
     const int BH = B * H, rows = BH * nq;
     uint16_t *vb16 = reinterpret_cast<uint16_t *>(ws);
-    size_t off = ((size_t)BH * nkp * HD * 2 + 255) & ~(size_t)255;
+    const size_t off = align256((size_t)BH * nkp * HD * 2);
     float *tk = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + off);
+    const bool v2 = rs_uses_v2(nkp, n_cand);
+    const int vt_stride = rs_vt_stride(nkp);
+    uint16_t *vbT = v2 ? nullptr
+                       : reinterpret_cast<uint16_t *>(reinterpret_cast<char *>(ws) +
+                                                      align256(off + (size_t)BH * n_cand * sizeof(float)));
     vbar_terms_kernel<T><<<dim3((nkp + 127) / 128, BH), 128, 0, st>>>((const T *)vbar, M, H, nkp, n_cand,
-                                                                       vb16, tk);
+                                                                       vb16, tk, vbT, vt_stride);
     Fracs fr;
     for (int i = 0; i < MAX_ITERS; ++i) fr.f[i] = i < n_iters ? fracs[i] : 0.0f;
     {
@@ -967,7 +1013,7 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
     set_smem_attr((const void *)kern, sm);
     kern<<<rows, SEL_NT, sm, st>>>((const T *)attn_full, vb16, tk, M, nts, H, nq, nkp, n_cand, n_iters,
                                    fr, track_best, drop, s, lists, counts, list_width, sink_blocks, lead,
-                                   status);
+                                   status, vbT, vt_stride);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }
 
