@@ -824,12 +824,28 @@ inline int pass_grid(long long tiles) {
 // ------------------------------------------------------------------ predict
 constexpr int PRED_NT = 256;
 
+// Sequential fp32 sum of x[0..n) in index order; the shared-memory loads of
+// a batch of 8 are issued before its additions.
+__device__ __forceinline__ float seq_sum(const float *x, int n) {
+    float s = 0.0f;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = x[j + u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) s = __fadd_rn(s, v[u]);
+    }
+    for (; j < n; ++j) s = __fadd_rn(s, x[j]);
+    return s;
+}
+
 // One CTA handles `rows` consecutive q-blocks of one head (rows <= 8, one
 // warp per row for the row-wise steps).
 template <typename T>
 __global__ void __launch_bounds__(PRED_NT) predict_kernel(
     const T *__restrict__ qbar, const T *__restrict__ kbar, int nq, int nkp, int n_cand,
-    int rows_per_cta, float scale, T *__restrict__ attn_full, T *__restrict__ attn_cond) {
+    int rows_per_cta, float scale, T *__restrict__ attn_full, T *__restrict__ attn_cond, int kbar_vec) {
     extern __shared__ float smem[];
     float *qs = smem;                               // rows x 64
     float *sc = qs + 8 * HD;                        // rows x nkp
@@ -844,12 +860,33 @@ __global__ void __launch_bounds__(PRED_NT) predict_kernel(
     for (int j = tid; j < nkp; j += PRED_NT) {
         float kv[HD];
         const T *kp = kbar + ((size_t)bh * nkp + j) * HD;
+        if (sizeof(T) == 2 && kbar_vec) {
+            // the row as 8 16-byte loads (kbar 16-byte aligned)
 #pragma unroll
-        for (int d = 0; d < HD; ++d) kv[d] = DT<T>::load(kp, d);
+            for (int c = 0; c < 8; ++c) {
+                const uint4 u = __ldg(reinterpret_cast<const uint4 *>(kp) + c);
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    kv[c * 8 + 2 * e] = __uint_as_float(w[e] << 16);
+                    kv[c * 8 + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int d = 0; d < HD; ++d) kv[d] = DT<T>::load(kp, d);
+        }
         for (int r = 0; r < nr; ++r) {
             float acc = 0.0f;
+            const float4 *q4 = reinterpret_cast<const float4 *>(qs + r * HD);
 #pragma unroll
-            for (int d = 0; d < HD; ++d) acc = __fmaf_rn(qs[r * HD + d], kv[d], acc);
+            for (int d4 = 0; d4 < HD / 4; ++d4) {
+                const float4 qv = q4[d4];
+                acc = __fmaf_rn(qv.x, kv[4 * d4], acc);
+                acc = __fmaf_rn(qv.y, kv[4 * d4 + 1], acc);
+                acc = __fmaf_rn(qv.z, kv[4 * d4 + 2], acc);
+                acc = __fmaf_rn(qv.w, kv[4 * d4 + 3], acc);
+            }
             acc = DT<T>::round(acc);
             sc[(size_t)r * nkp + j] = DT<T>::round(__fmul_rn(acc, scale));
         }
@@ -863,11 +900,7 @@ __global__ void __launch_bounds__(PRED_NT) predict_kernel(
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         for (int j = l; j < nkp; j += 32) x[j] = ress_expf(__fsub_rn(x[j], m));
         __syncwarp();
-        if (l == 0) {
-            float s = 0.0f;
-            for (int j = 0; j < nkp; ++j) s = __fadd_rn(s, x[j]);
-            rowsum[w] = s;
-        }
+        if (l == 0) rowsum[w] = seq_sum(x, nkp);
         __syncwarp();
         const float s = rowsum[w];
         const size_t ob = ((size_t)bh * nq + q0 + w) * nkp;
@@ -877,11 +910,7 @@ __global__ void __launch_bounds__(PRED_NT) predict_kernel(
             if (attn_full) DT<T>::store(attn_full, ob + j, a);
         }
         __syncwarp();
-        if (l == 0) {
-            float s2 = 0.0f;
-            for (int j = 0; j < n_cand; ++j) s2 = __fadd_rn(s2, x[j]);
-            rowsum[w] = clamp_min(DT<T>::round(s2), DT<T>::round(1e-6f));
-        }
+        if (l == 0) rowsum[w] = clamp_min(DT<T>::round(seq_sum(x, n_cand)), DT<T>::round(1e-6f));
         __syncwarp();
         const float s2 = rowsum[w];
         const size_t cb = ((size_t)bh * nq + q0 + w) * n_cand;
@@ -1057,7 +1086,7 @@ static int predict_t(const void *qbar, const void *kbar, int BH, int nq, int nkp
     set_smem_attr((const void *)kern, sm);
     dim3 grid((nq + rows - 1) / rows, BH);
     kern<<<grid, PRED_NT, sm, s>>>((const T *)qbar, (const T *)kbar, nq, nkp, n_cand, rows, 0.125f, (T *)attn_full,
-                                   (T *)attn_cond);
+                                   (T *)attn_cond, ((uintptr_t)kbar & 15) == 0 ? 1 : 0);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }
 
