@@ -551,6 +551,10 @@ __device__ __forceinline__ void fma2_chain_fwd(float &c0, float &c1, float a0, f
         : "f"(a0), "f"(a1), "f"(b));
 }
 __host__ __device__ __forceinline__ int rs2_vstride(int nkp) { return ((nkp + 63) / 64) * 64 + 8; }
+__host__ __device__ __forceinline__ int rs2_pd_len(int n_cand) {
+    const int n = (n_cand + 3) & ~3;
+    return n > 260 ? n : 260;
+}
 __device__ __forceinline__ float bfl(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bfh(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
@@ -714,6 +718,129 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
     gbar(g);
 }
 
+// The two selections of a restore-swap round in one pass sequence: selA =
+// top-mA of {i : drop[i]} and selB = top-mB of {i : !drop[i]} by key (larger
+// first, ties to the lower index), each exactly group_select_top_m's result.
+// The sets are disjoint, so every key feeds one of two histograms (histA in
+// the scratch, histB in `aux`, 256 + 2 ints of caller memory that is dead at
+// this point), and both sets share the element passes and the barriers; the
+// two radix scans run on the group's two warps side by side.
+__device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop, int n, int mA, int mB,
+                                        uint8_t *selA, uint8_t *selB, GroupScratch &sc, int *aux, int g, int t) {
+    int *histA = sc.hist, *histB = aux;
+    int *resB = aux + 256;  // bin, remaining of set B
+    const int chunk = (n + G_NT - 1) / G_NT;
+    const int i0 = t * chunk, i1 = min(n, i0 + chunk);
+    int nvA = 0, nvB = 0;
+    for (int i = i0; i < i1; ++i) {
+        if (drop[i]) ++nvA;
+        else ++nvB;
+    }
+    const int nv = gsum(nvA | (nvB << 16), sc.red, g, t);  // n < 2^16: the two counts do not mix
+    const int n_validA = nv & 0xFFFF, n_validB = nv >> 16;
+    if (mA < 0) mA = 0;
+    if (mB < 0) mB = 0;
+    const bool doneA = mA >= n_validA || mA == 0, doneB = mB >= n_validB || mB == 0;
+    uint32_t prefA = 0, prefB = 0, pmask = 0;
+    int remA = mA, remB = mB;
+    if (!(doneA && doneB)) {
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int b = t; b < 256; b += G_NT) {
+                histA[b] = 0;
+                histB[b] = 0;
+            }
+            gbar(g);
+            for (int j = 0; j < chunk; ++j) {
+                const int i = i0 + j;
+                int bin = -1;
+                if (i < i1) {
+                    const uint32_t k = key[i];
+                    if (drop[i]) {
+                        if (!doneA && (k & pmask) == prefA) bin = (int)((k >> shift) & 255u);
+                    } else if (!doneB && (k & pmask) == prefB) {
+                        bin = 256 + (int)((k >> shift) & 255u);
+                    }
+                }
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (bin >= 0 && (t & 31) == __ffs(peers) - 1)
+                    atomicAdd(bin < 256 ? &histA[bin] : &histB[bin - 256], __popc(peers));
+            }
+            gbar(g);
+            // warp 0 scans set A, warp 1 set B
+            const int w = t >> 5, l = t & 31;
+            const bool active = w == 0 ? !doneA : !doneB;
+            if (active) {
+                const int *hist = w == 0 ? histA : histB;
+                const int rem = w == 0 ? remA : remB;
+                int c[8], sum = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    c[j] = hist[255 - 8 * l - j];
+                    sum += c[j];
+                }
+                int x = sum;
+                for (int o = 1; o < 32; o <<= 1) {
+                    int y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (l >= o) x += y;
+                }
+                const int before = x - sum;
+                if (before < rem && rem <= x) {
+                    int acc = before;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (acc < rem && rem <= acc + c[j]) {
+                            if (w == 0) {
+                                sc.bin = 255 - 8 * l - j;
+                                sc.remaining = rem - acc;
+                            } else {
+                                resB[0] = 255 - 8 * l - j;
+                                resB[1] = rem - acc;
+                            }
+                        }
+                        acc += c[j];
+                    }
+                }
+            }
+            gbar(g);
+            if (!doneA) {
+                prefA |= ((uint32_t)sc.bin) << shift;
+                remA = sc.remaining;
+            }
+            if (!doneB) {
+                prefB |= ((uint32_t)resB[0]) << shift;
+                remB = resB[1];
+            }
+            pmask |= 255u << shift;
+            gbar(g);
+        }
+    }
+    int eqA = 0, eqB = 0;
+    for (int i = i0; i < i1; ++i) {
+        const uint32_t k = key[i];
+        if (drop[i]) eqA += (!doneA && k == prefA) ? 1 : 0;
+        else eqB += (!doneB && k == prefB) ? 1 : 0;
+    }
+    int tot;
+    const int bef = gscan_excl(eqA | (eqB << 16), sc.red, g, t, &tot);
+    int beforeA = bef & 0xFFFF, beforeB = bef >> 16;
+    for (int i = i0; i < i1; ++i) {
+        uint8_t a = 0, b = 0;
+        const uint32_t k = key[i];
+        if (drop[i]) {
+            if (doneA) a = mA > 0 ? 1 : 0;
+            else if (k > prefA) a = 1;
+            else if (k == prefA) { a = (beforeA < remA) ? 1 : 0; ++beforeA; }
+        } else {
+            if (doneB) b = mB > 0 ? 1 : 0;
+            else if (k > prefB) b = 1;
+            else if (k == prefB) { b = (beforeB < remB) ? 1 : 0; ++beforeB; }
+        }
+        selA[i] = a;
+        selB[i] = b;
+    }
+    gbar(g);
+}
+
 // g, Mg, G, K, J of the current drop set, for one group.  The chains run
 // over every candidate with Pd[k] = drop[k] ? P[k] : +0: an accumulator that
 // starts at +0 is left bit-for-bit unchanged by adding a +0 or -0 product in
@@ -786,7 +913,8 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     GroupScratch &S = *reinterpret_cast<GroupScratch *>(rb);
     float *P = reinterpret_cast<float *>(rb + ((sizeof(GroupScratch) + 15) & ~(size_t)15));
     float *Pd = P + ((nkp + 3) & ~3);  // 16-byte aligned: the chains read four weights at a time
-    float *ssq = Pd + ((n_cand + 3) & ~3);
+    // Pd doubles as the second histogram of the dual top-m selection (258 ints)
+    float *ssq = Pd + rs2_pd_len(n_cand);
     uint32_t *key = reinterpret_cast<uint32_t *>(ssq + n_cand);
     uint8_t *drop = reinterpret_cast<uint8_t *>(key + n_cand);
     uint8_t *best = drop + n_cand;
@@ -877,7 +1005,6 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
                 key[k] = order_key(knorm_quality(G, K, __fsub_rn(ssq[k], __fmul_rn(2.0f, r)), -P[k]));
                 ++nk;
             }
-            valid[k] = drop[k] ? 0 : 1;
         };
         for (int k0 = 4 * t; k0 < n_cand; k0 += 4 * G_NT) {
             float a[4];
@@ -894,8 +1021,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
         cnt = min(cnt, n_drop);
         cnt = min(cnt, n_kept);
         if (!beneficial) cnt = 0;
-        group_select_top_m(key, drop, n_cand, cnt, sel, S, g, t);
-        group_select_top_m(key, valid, n_cand, cnt, sel2, S, g, t);
+        group_select_top_m_dual(key, drop, n_cand, cnt, cnt, sel, sel2, S, reinterpret_cast<int *>(Pd), g, t);
         for (int k = t; k < n_cand; k += G_NT) drop[k] = (uint8_t)((drop[k] && !sel[k]) || sel2[k]);
         gbar(g);
     }
@@ -935,7 +1061,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
 
 static size_t rs2_row_bytes(int nkp, int n_cand) {
     size_t b = ((sizeof(GroupScratch) + 15) & ~(size_t)15) + (size_t)((nkp + 3) & ~3) * 4 +
-               (size_t)((n_cand + 3) & ~3) * 4 + (size_t)n_cand * (4 + 4 + 5);
+               (size_t)rs2_pd_len(n_cand) * 4 + (size_t)n_cand * (4 + 4 + 5);
     return (b + 15) & ~(size_t)15;
 }
 static size_t rs2_fixed_bytes(int nkp) { return (size_t)rs2_vstride(nkp) * HD * 2 + (size_t)HD * HD * 4; }
