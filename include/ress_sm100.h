@@ -192,7 +192,8 @@ int ress_restore_swap(int dtype, const void *attn_full, const void *vbar, const 
  * reference always allocates through torch.
  * Scratch comes from a static __device__ array of RESS_NOALLOC_SCRATCH_BYTES
  * (4 MiB) held by every GPU that loads the library until exit; problems
- * needing more (about BH*nkp*128 + BH*n_cand*4 bytes; cfg2 needs 1.4 MiB)
+ * needing more (about BH*nkp*128 + BH*n_cand*4 bytes, plus another BH*nkp*128
+ * for layers too large for the shared-memory kernel; cfg2 needs 1.4 MiB)
  * return RESS_E_SCRATCH without launching.  The first call on each device
  * looks the array's device address up (cudaGetSymbolAddress) with that
  * device current; make it before any stream capture.  Calls share the array:
