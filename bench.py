@@ -452,9 +452,10 @@ def run_ress(args):
                        "l2": "inputs larger than L2 (Q/K/V bf16 270 MB)", "sparsity": round(sparsity, 4)},
             "stages_ms": stages,
             "apply_hess_layer_ms": hess_ms,
-            # per step: pool_q, pool_kv, key_mean, kquant, predict, baseline, hess,
-            # vbar_terms, restore_swap, row_order, sparse_attn (this library's kernels)
-            "gpu_launches": 11 * args.steps,
+            # per step: pool_q, pool_kv1<K>, key_mean, kquant, pool_kv1<V>, predict,
+            # baseline, hess, vbar_terms, restore_swap, row_order, sparse_attn
+            # (this library's kernels)
+            "gpu_launches": 12 * args.steps,
             "roofline": {"bound": "tensor", "kernel": "sparse_attn_kernel", "achieved": achieved,
                          "peak": mixed_peak, "unit": "TFLOP/s", "frac": achieved / mixed_peak,
                          "traffic": ATTN_DRAM_BYTES_PER_LAUNCH * args.frames / N_FRAMES,
