@@ -407,13 +407,13 @@ __global__ void __launch_bounds__(POOL_NT) kquant_kernel(
 }
 
 // ------------------------------------------------------- bf16 layer passes
-// Persistent forms of the three passes for bf16 layers (the common case):
-// each CTA walks tiles grid-stride and loads tile t + gridDim.x into
-// registers before working on tile t, so the HBM reads of the next tile
-// overlap this tile's arithmetic; the int8 codes come two per packed-fp32
-// instruction (quant_code2).  Same outputs, bit for bit, as the per-tile
-// kernels above (which serve fp32 layers).
-constexpr int PASS_BLOCKS_PER_SM = 4;
+// The passes for bf16 layers (the common case), same outputs bit for bit as
+// the generic kernels above (which serve fp32 layers).  The int8 codes come
+// two per packed-fp32 instruction (quant_code2); token rows are found by
+// invariant division; the Q pass and the K and V pooling passes take one
+// tile per CTA (their sequential window sums end a tile, and a fresh CTA
+// hides that tail), the K quantisation is persistent and loads tile
+// t + gridDim.x into registers before quantising tile t.
 
 __device__ __forceinline__ uint4 ldg16(const uint16_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -815,10 +815,6 @@ inline int sm_count() {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
     if (dev >= 0 && dev < 64) cached[dev] = n;
     return n;
-}
-inline int pass_grid(long long tiles) {
-    const long long cap = (long long)sm_count() * PASS_BLOCKS_PER_SM;
-    return (int)(tiles < cap ? tiles : cap);
 }
 
 // ------------------------------------------------------------------ predict
