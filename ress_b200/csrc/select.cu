@@ -553,7 +553,7 @@ __device__ __forceinline__ void fma2_chain_fwd(float &c0, float &c1, float a0, f
 __host__ __device__ __forceinline__ int rs2_vstride(int nkp) { return ((nkp + 63) / 64) * 64 + 8; }
 __host__ __device__ __forceinline__ int rs2_pd_len(int n_cand) {
     const int n = (n_cand + 3) & ~3;
-    return n > 260 ? n : 260;
+    return n > 516 ? n : 516;  // also the selections' two histograms (2 x 256 + 2 ints)
 }
 __device__ __forceinline__ float bfl(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bfh(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
@@ -612,7 +612,6 @@ __device__ __forceinline__ void quad_chains(const uint16_t *vbT, int vstride, in
 __device__ __forceinline__ void gbar(int g) { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(G_NT) : "memory"); }
 
 struct GroupScratch {
-    int hist[256];
     int red[2];
     int bin, remaining;
     float vq[HD], Mvq[HD], g[HD], Mg[HD], Mgb[HD];
@@ -643,8 +642,9 @@ __device__ __forceinline__ int gscan_excl(int v, int *red, int g, int t, int *to
 }
 
 // block_select_top_m for one 64-thread group (same semantics).
+// hist: 256 ints of caller memory that is dead during the selection.
 __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, int n, int m, uint8_t *sel,
-                                   GroupScratch &sc, int g, int t) {
+                                   GroupScratch &sc, int *hist, int g, int t) {
     const int chunk = (n + G_NT - 1) / G_NT;
     const int i0 = t * chunk, i1 = min(n, i0 + chunk);
     int nv = 0;
@@ -660,7 +660,7 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
     uint32_t prefix = 0, pmask = 0;
     int rem = m;
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int b = t; b < 256; b += G_NT) sc.hist[b] = 0;
+        for (int b = t; b < 256; b += G_NT) hist[b] = 0;
         gbar(g);
         // warp-aggregated histogram: lanes holding the same digit add once
         for (int j = 0; j < chunk; ++j) {
@@ -671,13 +671,13 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
                 if (valid[i] && (k & pmask) == prefix) bin = (int)((k >> shift) & 255u);
             }
             const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (bin >= 0 && (t & 31) == __ffs(peers) - 1) atomicAdd(&sc.hist[bin], __popc(peers));
+            if (bin >= 0 && (t & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
         }
         gbar(g);
         if (t < 32) {
             int c[8], sum = 0;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) { c[j] = sc.hist[255 - 8 * t - j]; sum += c[j]; }
+            for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * t - j]; sum += c[j]; }
             int x = sum;
             for (int o = 1; o < 32; o <<= 1) {
                 int y = __shfl_up_sync(0xffffffffu, x, o);
@@ -721,14 +721,14 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
 // The two selections of a restore-swap round in one pass sequence: selA =
 // top-mA of {i : drop[i]} and selB = top-mB of {i : !drop[i]} by key (larger
 // first, ties to the lower index), each exactly group_select_top_m's result.
-// The sets are disjoint, so every key feeds one of two histograms (histA in
-// the scratch, histB in `aux`, 256 + 2 ints of caller memory that is dead at
-// this point), and both sets share the element passes and the barriers; the
-// two radix scans run on the group's two warps side by side.
+// The sets are disjoint, so every key feeds one of two histograms (histA and
+// histB in `aux`, 2 x 256 + 2 ints of caller memory that is dead at this
+// point), and both sets share the element passes and the barriers; the two
+// radix scans run on the group's two warps side by side.
 __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop, int n, int mA, int mB,
                                         uint8_t *selA, uint8_t *selB, GroupScratch &sc, int *aux, int g, int t) {
-    int *histA = sc.hist, *histB = aux;
-    int *resB = aux + 256;  // bin, remaining of set B
+    int *histA = aux, *histB = aux + 256;
+    int *resB = aux + 512;  // bin, remaining of set B
     const int chunk = (n + G_NT - 1) / G_NT;
     const int i0 = t * chunk, i1 = min(n, i0 + chunk);
     int nvA = 0, nvB = 0;
@@ -913,9 +913,10 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     GroupScratch &S = *reinterpret_cast<GroupScratch *>(rb);
     float *P = reinterpret_cast<float *>(rb + ((sizeof(GroupScratch) + 15) & ~(size_t)15));
     float *Pd = P + ((nkp + 3) & ~3);  // 16-byte aligned: the chains read four weights at a time
-    // Pd doubles as the second histogram of the dual top-m selection (258 ints)
-    float *ssq = Pd + rs2_pd_len(n_cand);
-    uint32_t *key = reinterpret_cast<uint32_t *>(ssq + n_cand);
+    // Pd doubles as the histograms of the top-m selections (dead while they run)
+    int *hist = reinterpret_cast<int *>(Pd);
+    uint16_t *ssq = reinterpret_cast<uint16_t *>(Pd + rs2_pd_len(n_cand));  // bf16-rounded values as bits
+    uint32_t *key = reinterpret_cast<uint32_t *>(ssq + ((n_cand + 7) & ~7));
     uint8_t *drop = reinterpret_cast<uint8_t *>(key + n_cand);
     uint8_t *best = drop + n_cand;
     uint8_t *valid = best + n_cand;
@@ -953,7 +954,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
         const float sq = bf16r(__fsqrt_rn(quad));
         const float sv = bf16r(__fmul_rn(P[k], sq));
         const float den = clamp_min(bf16r(__fsub_rn(1.0f, P[k])), eps4);
-        ssq[k] = bf16r(__fmul_rn(sv, sv));
+        ssq[k] = bf16bits(__fmul_rn(sv, sv));
         if (s_out) s_out[(size_t)row * n_cand + k] = bf16bits(sv);
         key[k] = order_key(bf16r(__fdiv_rn(sv, den)));
         valid[k] = 1;
@@ -968,7 +969,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     }
     gbar(g);
     const int nt = nts[row];
-    group_select_top_m(key, valid, n_cand, min(nt, n_cand), sel, S, g, t);
+    group_select_top_m(key, valid, n_cand, min(nt, n_cand), sel, S, hist, g, t);
     for (int k = t; k < n_cand; k += G_NT) drop[k] = sel[k] ? 0 : 1;
     gbar(g);
     if (track_best) {
@@ -997,12 +998,12 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
             const float tkk = bf16r(acc);
             const float r = bf16r(__fmul_rn(P[k], bf16r(__fsub_rn(tkk, tqb))));
             if (drop[k]) {
-                const float rq = knorm_quality(G, K, __fadd_rn(__fmul_rn(2.0f, r), ssq[k]), P[k]);
+                const float rq = knorm_quality(G, K, __fadd_rn(__fmul_rn(2.0f, r), bf16_from_bits(ssq[k])), P[k]);
                 key[k] = order_key(rq);
                 ben |= (rq > 0.0f) ? 1 : 0;
                 ++nd;
             } else {
-                key[k] = order_key(knorm_quality(G, K, __fsub_rn(ssq[k], __fmul_rn(2.0f, r)), -P[k]));
+                key[k] = order_key(knorm_quality(G, K, __fsub_rn(bf16_from_bits(ssq[k]), __fmul_rn(2.0f, r)), -P[k]));
                 ++nk;
             }
         };
@@ -1021,7 +1022,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
         cnt = min(cnt, n_drop);
         cnt = min(cnt, n_kept);
         if (!beneficial) cnt = 0;
-        group_select_top_m_dual(key, drop, n_cand, cnt, cnt, sel, sel2, S, reinterpret_cast<int *>(Pd), g, t);
+        group_select_top_m_dual(key, drop, n_cand, cnt, cnt, sel, sel2, S, hist, g, t);
         for (int k = t; k < n_cand; k += G_NT) drop[k] = (uint8_t)((drop[k] && !sel[k]) || sel2[k]);
         gbar(g);
     }
@@ -1060,8 +1061,10 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
 }
 
 static size_t rs2_row_bytes(int nkp, int n_cand) {
+    // scratch, P (fp32), Pd (fp32, also the selection histograms), s^2 (bf16
+    // bits), keys (u32), five byte flags per candidate
     size_t b = ((sizeof(GroupScratch) + 15) & ~(size_t)15) + (size_t)((nkp + 3) & ~3) * 4 +
-               (size_t)rs2_pd_len(n_cand) * 4 + (size_t)n_cand * (4 + 4 + 5);
+               (size_t)rs2_pd_len(n_cand) * 4 + (size_t)((n_cand + 7) & ~7) * 2 + (size_t)n_cand * (4 + 5);
     return (b + 15) & ~(size_t)15;
 }
 static size_t rs2_fixed_bytes(int nkp) { return (size_t)rs2_vstride(nkp) * HD * 2 + (size_t)HD * HD * 4; }
