@@ -278,7 +278,10 @@ def run_ress(args):
     out = torch.empty(1, L.H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=device)
 
     def eager_step():
-        return LY.global_layer(S["q"], S["k"], S["v"], L, S["budget"], S["order"], out=out, shard=S["shard"])
+        # attn_split=None: with the heads split over many GPUs a rank's launch has few
+        # rows, and rows that keep nearly every block run as two halves
+        return LY.global_layer(S["q"], S["k"], S["v"], L, S["budget"], S["order"], out=out, shard=S["shard"],
+                               attn_split=None)
 
     def barrier():
         if ws > 1:
@@ -324,7 +327,7 @@ def run_ress(args):
     lists, counts = res.lists, res.counts
 
     def attn():
-        K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out, out_layout=L)
+        K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out, out_layout=L, split=None)
 
     for _ in range(3):
         attn()
@@ -357,7 +360,7 @@ def run_ress(args):
         ev[2].record(stream)
         r = K.restore_swap(af, vbar, S["order"].M, nts.view(-1), L.n_cand, sink_blocks=L.sink_blocks)
         ev[3].record(stream)
-        K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L)
+        K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L, split=None)
         ev[4].record(stream)
         ev[4].synchronize()
     for i, name in enumerate(["score_quant", "predict_budget", "restore_swap", "sparse_attn"]):
@@ -397,7 +400,8 @@ def run_ress(args):
             sl["in_ready"].record(s_in)
         stream.wait_event(sl["in_ready"])
         stream.wait_event(sl["drained"])
-        LY.global_layer(sl["q"], sl["k"], sl["v"], L, S["budget"], S["order"], out=sl["o"], shard=S["shard"])
+        LY.global_layer(sl["q"], sl["k"], sl["v"], L, S["budget"], S["order"], out=sl["o"], shard=S["shard"],
+                        attn_split=None)
         sl["used"].record(stream)
         sl["done"].record(stream)
         with torch.cuda.stream(s_out):

@@ -283,6 +283,25 @@ int ress_sparse_attn_sched(const int8_t *q8, const float *qscale, const int8_t *
                            long long out_sh, long long out_st, int out_hw, int out_special,
                            int32_t *status, int32_t *row_order, ress_stream_t stream);
 
+/* ress_sparse_attn_sched for launches with few rows (a head split over many
+ * GPUs), where rows that keep nearly every block would otherwise set the
+ * kernel time on their own: a row longer than split_chunk blocks runs as
+ * ceil(count / split_chunk) pieces (at most 4) of its list on separate CTAs,
+ * and the piece that finishes last merges them in piece order (softmax
+ * maxima and sums combined in fp32).  Scratch, all caller-allocated:
+ * item_order 4*rows int32; partial rows*4*128*68 fp32, 16-byte aligned;
+ * row_done rows int32, zero before the first call (every call leaves it
+ * zero).  P is rounded to fp16 per piece, so split rows agree with
+ * ress_sparse_attn within the attention tolerance rather than bit for bit.
+ * No counterpart in the reference (SpargeAttn runs one CTA per row).
+ * Widths above 16384: RESS_E_SHAPE. */
+int ress_sparse_attn_split(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
+                           const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
+                           const int32_t *counts, int list_width, float sm_scale, float *out,
+                           long long out_sh, long long out_st, int out_hw, int out_special,
+                           int32_t *status, int32_t *item_order, int split_chunk, float *partial,
+                           int32_t *row_done, ress_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

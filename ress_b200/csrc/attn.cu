@@ -341,7 +341,29 @@ struct Bars {
     uint64_t s_done, pv_done;
     uint32_t tmem_base;
     int abort_flag;
+    int merge;  // split rows: this CTA finished second and merges the two halves
 };
+
+// Split rows: a row longer than the launch's piece size runs as up to
+// SPLIT_MAX pieces of its list on separate CTAs.  Each piece writes, per
+// query, its unnormalised O (64), running maximum m (log2 units) and sum l
+// into a slot of PART_ROW floats per query (16-byte aligned rows); the piece
+// that finishes last merges all of them in piece order.
+constexpr int SPLIT_MAX = 2;
+constexpr int PART_ROW = HD + 4;
+constexpr size_t PART_SLOT = (size_t)128 * PART_ROW;  // floats per (row, piece)
+// Pieces of a row of `full` blocks for piece size `chunk` (all non-empty),
+// and the size of each but possibly the last.
+__host__ __device__ __forceinline__ int split_size(int full, int chunk) {
+    int pieces = (full + chunk - 1) / chunk;
+    pieces = pieces < 1 ? 1 : (pieces > SPLIT_MAX ? SPLIT_MAX : pieces);
+    return (full + pieces - 1) / pieces;
+}
+__host__ __device__ __forceinline__ int split_pieces(int full, int chunk) {
+    if (full <= chunk) return 1;
+    const int sz = split_size(full, chunk);
+    return (full + sz - 1) / sz;
+}
 
 __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -349,7 +371,8 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     const float *__restrict__ kscale, int nqb, int nkb, int Tq, int Tk, const int32_t *__restrict__ lists,
     const int32_t *__restrict__ counts, int list_width, float sm_scale_log2, float *__restrict__ out,
     long long out_sh, long long out_st, int out_hw, int out_special, int32_t *__restrict__ status,
-    const int32_t *__restrict__ row_order) {
+    const int32_t *__restrict__ row_order, int split_chunk, float *__restrict__ partial,
+    int32_t *__restrict__ row_done) {
     extern __shared__ unsigned char dyn_raw[];
     __shared__ Bars B;
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)dyn_raw + 1023) & ~(uintptr_t)1023);
@@ -367,10 +390,27 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // rows in descending block count when an order is given: the long rows of
     // heavily budgeted heads start first and the last wave is short
-    const int row = row_order != nullptr ? row_order[blockIdx.x] : (int)blockIdx.x;
+    // Split launches (partial != nullptr): the grid covers (row, piece) items,
+    // row_order lists them as SPLIT_MAX * row + piece; a row longer than
+    // split_chunk blocks runs as split_pieces() pieces of its list on as many
+    // CTAs, other rows on their piece-0 CTA alone.
+    const bool split_launch = partial != nullptr;
+    int row, piece = 0;
+    if (split_launch) {
+        const int item = row_order[blockIdx.x];
+        row = item / SPLIT_MAX;
+        piece = item - row * SPLIT_MAX;
+    } else {
+        row = row_order != nullptr ? row_order[blockIdx.x] : (int)blockIdx.x;
+    }
+    const int full_cnt = min(counts[row], list_width);
+    const int pieces = split_launch ? split_pieces(max(full_cnt, 0), split_chunk) : 1;
+    if (piece >= pieces) return;  // an empty item: the whole CTA leaves before any barrier
+    const bool split = pieces > 1;
+    const int psz = split ? split_size(full_cnt, split_chunk) : full_cnt;
+    const int cnt = split ? min(psz, full_cnt - piece * psz) : full_cnt;
+    const int32_t *lst = lists + (size_t)row * list_width + (size_t)piece * (split ? psz : 0);
     const int bh = row / nqb, qb = row - bh * nqb;
-    const int cnt = min(counts[row], list_width);
-    const int32_t *lst = lists + (size_t)row * list_width;
     volatile int *abort_flag = &B.abort_flag;
 
     if (threadIdx.x == 0) {
@@ -591,7 +631,15 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             ok = wait_bar_warp(&B.o_full[(cnt - 1) % NP], ((cnt - 1) / NP) & 1, abort_flag, status);
             fence_after();
         }
-        const int t = qb * 128 + r;
+        // the row, piece and their derived indices are re-read here rather
+        // than held in registers through the block loop
+        int row_e = row_order != nullptr ? row_order[blockIdx.x] : (int)blockIdx.x, piece_e = 0;
+        if (split_launch) {
+            piece_e = row_e % SPLIT_MAX;
+            row_e /= SPLIT_MAX;
+        }
+        const int bh_e = row_e / nqb, qb_e = row_e - bh_e * nqb;
+        const int t = qb_e * 128 + r;
         float l = 0.0f;  // sum(P) from the ones columns of O
         if (ok && cnt > 0) {
             uint32_t o16[16];
@@ -599,25 +647,97 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             tmem_wait_ld();
             l = __uint_as_float(o16[0]);
         }
-        const float inv = (ok && cnt > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
         const long long tt = (long long)(t / out_hw) * (out_hw + out_special) + out_special + (t % out_hw);
-        float *dst = out + (size_t)bh * out_sh + tt * out_st;
+        float *dst = out + (size_t)bh_e * out_sh + tt * out_st;
+        const int pieces_e = split_launch ? split_pieces(max(min(__ldg(&counts[row_e]), list_width), 0), split_chunk) : 1;
+        if (pieces_e == 1) {
+            const float inv = (ok && cnt > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            uint32_t o16[16];
-            if (ok && cnt > 0) {
-                tmem_ld16(tO + ch * 16 + lane_addr, o16);
-                tmem_wait_ld();
-            } else {
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t o16[16];
+                if (ok && cnt > 0) {
+                    tmem_ld16(tO + ch * 16 + lane_addr, o16);
+                    tmem_wait_ld();
+                } else {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) o16[i] = 0u;
+                    for (int i = 0; i < 16; ++i) o16[i] = 0u;
+                }
+                if (t < Tq) {
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4)
+                        *reinterpret_cast<float4 *>(dst + ch * 16 + i) =
+                            make_float4(__uint_as_float(o16[i]) * inv, __uint_as_float(o16[i + 1]) * inv,
+                                        __uint_as_float(o16[i + 2]) * inv, __uint_as_float(o16[i + 3]) * inv);
+                }
             }
-            if (t < Tq) {
+        } else {
+            // this piece's partial (O unnormalised, m, l) for query r
+            float *mine = partial + ((size_t)row_e * SPLIT_MAX + piece_e) * PART_SLOT + (size_t)r * PART_ROW;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t o16[16];
+                if (ok) {
+                    tmem_ld16(tO + ch * 16 + lane_addr, o16);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o16[i] = 0u;
+                }
 #pragma unroll
                 for (int i = 0; i < 16; i += 4)
-                    *reinterpret_cast<float4 *>(dst + ch * 16 + i) =
-                        make_float4(__uint_as_float(o16[i]) * inv, __uint_as_float(o16[i + 1]) * inv,
-                                    __uint_as_float(o16[i + 2]) * inv, __uint_as_float(o16[i + 3]) * inv);
+                    *reinterpret_cast<float4 *>(mine + ch * 16 + i) =
+                        make_float4(__uint_as_float(o16[i]), __uint_as_float(o16[i + 1]), __uint_as_float(o16[i + 2]),
+                                    __uint_as_float(o16[i + 3]));
+            }
+            mine[HD] = m;
+            mine[HD + 1] = ok ? l : 0.0f;
+            __threadfence();
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
+            if (r == 0) {
+                const int prev = atomicAdd(&row_done[row_e], 1);
+                B.merge = prev == pieces_e - 1;
+                if (prev == pieces_e - 1) row_done[row_e] = 0;  // every piece in: ready for the next launch
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (B.merge) {
+                // the last piece to finish merges all of them, in piece order
+                __threadfence();
+                const float *base = partial + (size_t)row_e * SPLIT_MAX * PART_SLOT + (size_t)r * PART_ROW;
+                float mp[SPLIT_MAX], lp[SPLIT_MAX];
+                float mm = -INFINITY;
+#pragma unroll
+                for (int p = 0; p < SPLIT_MAX; ++p) {
+                    if (p < pieces_e) {
+                        mp[p] = __ldcg(base + p * PART_SLOT + HD);
+                        lp[p] = __ldcg(base + p * PART_SLOT + HD + 1);
+                        if (lp[p] > 0.0f) mm = fmaxf(mm, mp[p]);
+                    }
+                }
+                float w[SPLIT_MAX], lsum = 0.0f;
+#pragma unroll
+                for (int p = 0; p < SPLIT_MAX; ++p) {
+                    w[p] = (p < pieces_e && lp[p] > 0.0f) ? ex2(mp[p] - mm) : 0.0f;
+                    if (p < pieces_e) lsum = fmaf(lp[p], w[p], lsum);
+                }
+                const float inv = (ok && lsum > 0.0f) ? 1.0f / lsum : 0.0f;
+                if (t < Tq) {
+#pragma unroll
+                    for (int i = 0; i < HD; i += 4) {
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int p = 0; p < SPLIT_MAX; ++p) {
+                            if (p < pieces_e) {
+                                const float4 ov = __ldcg(reinterpret_cast<const float4 *>(base + p * PART_SLOT + i));
+                                acc.x = fmaf(ov.x, w[p], acc.x);
+                                acc.y = fmaf(ov.y, w[p], acc.y);
+                                acc.z = fmaf(ov.z, w[p], acc.z);
+                                acc.w = fmaf(ov.w, w[p], acc.w);
+                            }
+                        }
+                        *reinterpret_cast<float4 *>(dst + i) =
+                            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+                    }
+                }
             }
         }
     }
@@ -651,6 +771,39 @@ __global__ void __launch_bounds__(ORDER_NT) row_order_kernel(const int32_t *__re
     __syncthreads();
     for (int r = threadIdx.x; r < rows; r += ORDER_NT)
         order[atomicAdd(&pos[min(max(counts[r], 0), list_width)], 1)] = r;
+}
+
+// Split launches: (row, piece) items sorted by descending length (pieces of
+// a row longer than split_chunk cover consecutive parts of its list; items
+// past a row's piece count are empty, sort last and exit at once).
+__global__ void __launch_bounds__(ORDER_NT) item_order_kernel(const int32_t *__restrict__ counts, int rows,
+                                                               int list_width, int split_chunk,
+                                                               int32_t *__restrict__ order) {
+    extern __shared__ int pos[];  // list_width + 1 bins
+    const int nb = list_width + 1;
+    auto len = [&](int item) {
+        const int row = item / SPLIT_MAX, p = item - row * SPLIT_MAX;
+        const int c = min(max(counts[row], 0), list_width);
+        const int n = split_pieces(c, split_chunk);
+        if (p >= n) return 0;
+        if (n == 1) return c;
+        const int sz = split_size(c, split_chunk);
+        return min(sz, c - p * sz);
+    };
+    for (int c = threadIdx.x; c < nb; c += ORDER_NT) pos[c] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < SPLIT_MAX * rows; i += ORDER_NT) atomicAdd(&pos[len(i)], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int c = list_width; c >= 0; --c) {
+            const int n = pos[c];
+            pos[c] = acc;
+            acc += n;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < SPLIT_MAX * rows; i += ORDER_NT) order[atomicAdd(&pos[len(i)], 1)] = i;
 }
 
 // ------------------------------------------------------------- host side
@@ -688,7 +841,7 @@ static int sparse_attn_impl(const int8_t *q8, const float *qscale, const int8_t 
                             const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
                             const int32_t *counts, int list_width, float sm_scale, float *out, long long out_sh,
                             long long out_st, int out_hw, int out_special, int32_t *status, int32_t *row_order,
-                            ress_stream_t stream) {
+                            int split_chunk, float *partial, int32_t *row_done, ress_stream_t stream) {
     if (!q8 || !qscale || !k8 || !kscale || !v16 || !lists || !counts || !out || !status) return RESS_E_ARG;
     if (BH <= 0 || Tq <= 0 || Tk <= 0 || list_width <= 0 || out_hw <= 0 || out_special < 0) return RESS_E_ARG;
     if (((uintptr_t)q8 | (uintptr_t)k8 | (uintptr_t)v16) & 15) return RESS_E_ARG;
@@ -701,8 +854,13 @@ static int sparse_attn_impl(const int8_t *q8, const float *qscale, const int8_t 
         return RESS_E_NO_DEVICE;
     const int nqb = (Tq + 127) / 128, nkb = (Tk + 63) / 64;
     const int rows = BH * nqb;
-    if (row_order != nullptr && list_width <= attn::ORDER_MAX_WIDTH) {
-        const size_t sm = (size_t)(list_width + 1) * sizeof(int);
+    const bool split = partial != nullptr;
+    const size_t sm = (size_t)(list_width + 1) * sizeof(int);
+    if (split) {
+        set_smem_attr((const void *)attn::item_order_kernel, sm);
+        attn::item_order_kernel<<<1, attn::ORDER_NT, sm, (cudaStream_t)stream>>>(counts, rows, list_width,
+                                                                                split_chunk, row_order);
+    } else if (row_order != nullptr && list_width <= attn::ORDER_MAX_WIDTH) {
         set_smem_attr((const void *)attn::row_order_kernel, sm);
         attn::row_order_kernel<<<1, attn::ORDER_NT, sm, (cudaStream_t)stream>>>(counts, rows, list_width, row_order);
     } else {
@@ -710,9 +868,10 @@ static int sparse_attn_impl(const int8_t *q8, const float *qscale, const int8_t 
     }
     set_smem_attr((const void *)attn::sparse_attn_kernel, attn::SMEM_BYTES);
     const float log2e = 1.4426950408889634f;
-    attn::sparse_attn_kernel<<<rows, attn::NT, attn::SMEM_BYTES, (cudaStream_t)stream>>>(
+    attn::sparse_attn_kernel<<<split ? attn::SPLIT_MAX * rows : rows, attn::NT, attn::SMEM_BYTES,
+                               (cudaStream_t)stream>>>(
         tq, tk, tv, qscale, kscale, nqb, nkb, Tq, Tk, lists, counts, list_width, sm_scale * log2e, out, out_sh,
-        out_st, out_hw, out_special, status, row_order);
+        out_st, out_hw, out_special, status, row_order, split_chunk, partial, row_done);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }
 
@@ -722,7 +881,7 @@ extern "C" int ress_sparse_attn(const int8_t *q8, const float *qscale, const int
                                 long long out_sh, long long out_st, int out_hw, int out_special,
                                 int32_t *status, ress_stream_t stream) {
     return sparse_attn_impl(q8, qscale, k8, kscale, v16, BH, Tq, Tk, lists, counts, list_width, sm_scale, out,
-                            out_sh, out_st, out_hw, out_special, status, nullptr, stream);
+                            out_sh, out_st, out_hw, out_special, status, nullptr, 0, nullptr, nullptr, stream);
 }
 
 extern "C" int ress_sparse_attn_sched(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
@@ -732,5 +891,19 @@ extern "C" int ress_sparse_attn_sched(const int8_t *q8, const float *qscale, con
                                       int32_t *status, int32_t *row_order, ress_stream_t stream) {
     if (!row_order) return RESS_E_ARG;
     return sparse_attn_impl(q8, qscale, k8, kscale, v16, BH, Tq, Tk, lists, counts, list_width, sm_scale, out,
-                            out_sh, out_st, out_hw, out_special, status, row_order, stream);
+                            out_sh, out_st, out_hw, out_special, status, row_order, 0, nullptr, nullptr, stream);
+}
+
+extern "C" int ress_sparse_attn_split(const int8_t *q8, const float *qscale, const int8_t *k8, const float *kscale,
+                                      const uint16_t *v16, int BH, int Tq, int Tk, const int32_t *lists,
+                                      const int32_t *counts, int list_width, float sm_scale, float *out,
+                                      long long out_sh, long long out_st, int out_hw, int out_special,
+                                      int32_t *status, int32_t *item_order, int split_chunk, float *partial,
+                                      int32_t *row_done, ress_stream_t stream) {
+    if (!item_order || !partial || !row_done || split_chunk < 1) return RESS_E_ARG;
+    if (list_width > attn::ORDER_MAX_WIDTH) return RESS_E_SHAPE;
+    if ((uintptr_t)partial & 15) return RESS_E_ARG;
+    return sparse_attn_impl(q8, qscale, k8, kscale, v16, BH, Tq, Tk, lists, counts, list_width, sm_scale, out,
+                            out_sh, out_st, out_hw, out_special, status, item_order, split_chunk, partial,
+                            row_done, stream);
 }

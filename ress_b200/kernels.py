@@ -360,11 +360,33 @@ def lists_to_map(lists, counts, width):
     return m[:, :width]
 
 
+_SM_COUNT = {}
+
+
+def _sm_count(dev) -> int:
+    i = dev.index if dev.index is not None else torch.cuda.current_device()
+    if i not in _SM_COUNT:
+        _SM_COUNT[i] = torch.cuda.get_device_properties(i).multi_processor_count
+    return _SM_COUNT[i]
+
+
+# A launch with fewer rows than this many waves of CTAs (two per SM) splits
+# its long rows (split=None); with more, the descending-length schedule alone
+# keeps the last wave short.
+SPLIT_WAVES = 3
+SPLIT_MAX = 2  # pieces per row at most (attn.cu)
+
+
 def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout=None, sm_scale=None,
-                schedule=True):
+                schedule=True, split=False):
     """Block-sparse attention.  q8 (BH, Tq, 64); k8/v16 (BH, Tk, 64).
     out: fp32 tensor; with out_layout (a Layout) rows land at their full-layout
-    positions of a (B, H, frames*(special+hw), 64) tensor."""
+    positions of a (B, H, frames*(special+hw), 64) tensor.
+    split: False (default) runs one CTA per row, the same bits whatever the
+    launch; None lets launches of few rows (under SPLIT_WAVES waves) run rows
+    longer than a quarter of the list width as up to four pieces on separate
+    CTAs (outputs within the attention tolerance of the unsplit launch); an
+    int forces that piece size."""
     _dev_ok(q8, k8, v16, lists, counts)
     BH, Tq, _ = q8.shape
     Tk = k8.shape[1]
@@ -384,6 +406,20 @@ def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(HD)
     lw = lists.shape[-1]
+    rows = counts.numel()
+    if split is None:
+        few = schedule and rows < SPLIT_WAVES * 2 * _sm_count(dev) and lw <= 16384
+        split = max(32, (lw + SPLIT_MAX - 1) // SPLIT_MAX) if few else False
+    if split is not False:
+        item_order = torch.empty(SPLIT_MAX * rows, dtype=torch.int32, device=dev)
+        partial = torch.empty(rows * SPLIT_MAX * 128 * 68, dtype=torch.float32, device=dev)
+        row_done = torch.zeros(rows, dtype=torch.int32, device=dev)
+        check(_lib.load().ress_sparse_attn_split(_ptr(q8), _ptr(qscale), _ptr(k8), _ptr(kscale), _ptr(v16), BH, Tq,
+                                                 Tk, _ptr(lists), _ptr(counts), lw, ctypes.c_float(sm_scale), _ptr(out),
+                                                 o_sh, o_st, o_hw, o_sp, _ptr(status_word(dev)), _ptr(item_order),
+                                                 int(split), _ptr(partial), _ptr(row_done), _stream(dev)),
+              "ress_sparse_attn_split")
+        return out
     if schedule:
         # rows launched in descending kept-block count (same bits as the plain order)
         order = torch.empty(counts.numel(), dtype=torch.int32, device=dev)

@@ -193,11 +193,14 @@ def select_blocks(attn_full, attn_cond, vbar, B: int, H: int, nq: int, n_cand: i
 def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSpec, *,
                  num_to_select: torch.Tensor | None = None, budget_fn=None, keep_pooled: bool = False,
                  lead_blocks: int = 0, out: torch.Tensor | None = None,
-                 shard: HeadShard | None = None, joint_select_fn=None, map_hook=None) -> LayerResult:
+                 shard: HeadShard | None = None, joint_select_fn=None, map_hook=None,
+                 attn_split=False) -> LayerResult:
     """Run one sparse global-attention layer.  q, k, v: (B, H, N*P, 64) CUDA,
     float32 or bfloat16.  Exactly one of ``budget``, ``num_to_select`` (a
     (B, H, nq) tensor) or ``budget_fn`` (callable(attn_cond) -> (B, H, nq))
-    decides the per-row block count."""
+    decides the per-row block count.  ``attn_split`` is the attention's
+    ``split`` option (kernels.sparse_attn): None lets a layer with few rows
+    (a head split over many GPUs) spread its longest rows over two CTAs."""
     dev = q.device
     if k.stride() != v.stride():
         v = v.contiguous()
@@ -229,7 +232,7 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
         lists, counts = K.map_to_lists(fm.reshape(-1, width))
         if out is None:
             out = torch.empty(B, H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=dev)
-        K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out, out_layout=L)
+        K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out, out_layout=L, split=attn_split)
         main.wait_stream(side)
         if x_special is not None:
             if not capturing:
@@ -249,7 +252,7 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
         r = dict(lists=lists, counts=counts)
     if out is None:
         out = torch.empty(B, H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=dev)
-    K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L)
+    K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L, split=attn_split)
     main.wait_stream(side)
     if x_special is not None:
         if not capturing:

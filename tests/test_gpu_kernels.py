@@ -295,6 +295,46 @@ def test_sparse_attention_random_maps(density):
     assert e.mean().item() < 1e-3, e.mean().item()
 
 
+@pytest.mark.parametrize("chunk", [8, 30])
+def test_split_rows_match_oracle_and_unsplit(chunk):
+    """ress_sparse_attn_split: rows longer than `chunk` key blocks run as up
+    to four pieces of their list on separate CTAs, merged by the piece that
+    finishes last.  Random keep lists with a ragged key tail (47 key blocks:
+    at chunk 8 most rows split into four pieces, at chunk 30 into two):
+    sampled rows within 2e-2 max / 1e-3 mean abs of the fp64 oracle, every
+    row within 2e-3 of the one-CTA-per-row launch, and a second call on the
+    same scratch (the per-row counters must be left at zero) gives the same
+    bits as the first."""
+    g = torch.Generator().manual_seed(chunk)
+    T = 3000
+    q, k, v = (torch.randn(1, 4, T, 64, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
+    L = K.Layout.plain(q)
+    _, q8, qs = K.pool_quant_q(q, L, pool=False)
+    _, _, k8, ks, v16, _ = K.pool_quant_kv(k, v, L, pool=False)
+    m = torch.rand(4 * L.nq, L.nkb, generator=g) < 0.7
+    m[:, 0] = True
+    m[::5, 1:] = False  # some one-block rows, never split
+    lists, counts = K.map_to_lists(m.cuda())
+    plain = K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, split=False)
+    a = K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, split=chunk)
+    b = K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, split=chunk)
+    torch.cuda.synchronize()
+    K.check_status()
+    assert int((counts > chunk).sum()) > 10
+    assert torch.equal(a, b)
+    assert (a - plain).abs().max().item() < 2e-3
+    samples = [(h, bq) for h in range(4) for bq in (0, 7, L.nq - 1)]
+    ref = oracle.sparse_attn_rows(q8.cpu(), qs.cpu(), k8.cpu(), ks.cpu(), v16.cpu().float(),
+                                  lists.view(4, L.nq, -1).cpu(), counts.view(4, L.nq).cpu(), samples)
+    errs = []
+    for i, (h, bq) in enumerate(samples):
+        n = min(128, T - bq * 128)
+        errs.append((a[h, bq * 128: bq * 128 + n].cpu() - ref[i, :n]).abs().reshape(-1))
+    e = torch.cat(errs)
+    assert e.max().item() < 2e-2, e.max().item()
+    assert e.mean().item() < 1e-3, e.mean().item()
+
+
 def test_scale_division_exhaustive():
     """The quantisers divide by RN(amax/127) with a reciprocal and one fma
     correction; over every fp16 amax and every fp16 |x| <= amax it must give
