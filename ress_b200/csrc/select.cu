@@ -532,12 +532,12 @@ __global__ void __launch_bounds__(SEL_NT) map_lists_kernel(const uint8_t *__rest
 //     on distinct banks (rows 16 bytes apart modulo 128), and
 //   - a per-candidate pass (thread p takes four adjacent candidates, an FMA
 //     chain over the 64 dimensions each) reads the four with one 8-byte load.
-// One CTA processes up to 8 q-block rows of that head, one 64-thread group
-// (two warps, named barrier 1 + g) per row.  Operation order is that of
+// One CTA processes up to 8 q-block rows of that head, one group of GT
+// threads (64, or 128 for launches with few rows; named barrier 1 + g) per
+// row.  Operation order is that of
 // restore_swap_kernel / the oracle; only the placement of data changes.
 // (Measured before the transposition: the drift chains' per-element address
 // arithmetic and 2-byte loads were ~65 % of the kernel's instructions.)
-constexpr int G_NT = 64;
 // (d0, d1) = (a0 * b + c0, a1 * b + c1): two independent IEEE fp32 FMAs in one
 // issue slot (fma.rn.f32x2); each chain gets exactly the bits of __fmaf_rn.
 __device__ __forceinline__ void fma2_chain_fwd(float &c0, float &c1, float a0, float a1, float b) {
@@ -609,24 +609,30 @@ __device__ __forceinline__ void quad_chains(const uint16_t *vbT, int vstride, in
 }
 
 
-__device__ __forceinline__ void gbar(int g) { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(G_NT) : "memory"); }
+template <int GT>
+__device__ __forceinline__ void gbar(int g) { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(GT) : "memory"); }
 
 struct GroupScratch {
-    int red[2];
+    int red[4];
     int bin, remaining;
     float vq[HD], Mvq[HD], g[HD], Mg[HD], Mgb[HD];
     float tm, sum_pd, G, K, J, bestJ, tqb, tqs;
     int flag;
 };
 
+template <int GT>
 __device__ __forceinline__ int gsum(int v, int *red, int g, int t) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    gbar(g);
+    gbar<GT>(g);
     if ((t & 31) == 0) red[t >> 5] = v;
-    gbar(g);
-    return red[0] + red[1];
+    gbar<GT>(g);
+    int s = 0;
+#pragma unroll
+    for (int w = 0; w < GT / 32; ++w) s += red[w];
+    return s;
 }
 
+template <int GT>
 __device__ __forceinline__ int gscan_excl(int v, int *red, int g, int t, int *total) {
     const int l = t & 31, w = t >> 5;
     int x = v;
@@ -634,34 +640,41 @@ __device__ __forceinline__ int gscan_excl(int v, int *red, int g, int t, int *to
         int y = __shfl_up_sync(0xffffffffu, x, o);
         if (l >= o) x += y;
     }
-    gbar(g);
+    gbar<GT>(g);
     if (l == 31) red[w] = x;
-    gbar(g);
-    *total = red[0] + red[1];
-    return (w == 1 ? red[0] : 0) + x - v;
+    gbar<GT>(g);
+    int tot = 0, before = 0;
+#pragma unroll
+    for (int i = 0; i < GT / 32; ++i) {
+        if (i < w) before += red[i];
+        tot += red[i];
+    }
+    *total = tot;
+    return before + x - v;
 }
 
-// block_select_top_m for one 64-thread group (same semantics).
+// block_select_top_m for one group of GT threads (same semantics).
 // hist: 256 ints of caller memory that is dead during the selection.
+template <int GT>
 __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, int n, int m, uint8_t *sel,
                                    GroupScratch &sc, int *hist, int g, int t) {
-    const int chunk = (n + G_NT - 1) / G_NT;
+    const int chunk = (n + GT - 1) / GT;
     const int i0 = t * chunk, i1 = min(n, i0 + chunk);
     int nv = 0;
     for (int i = i0; i < i1; ++i) nv += valid[i] ? 1 : 0;
-    const int n_valid = gsum(nv, sc.red, g, t);
+    const int n_valid = gsum<GT>(nv, sc.red, g, t);
     if (m < 0) m = 0;
     if (m >= n_valid || m == 0) {
         const bool all = m > 0;
         for (int i = i0; i < i1; ++i) sel[i] = (all && valid[i]) ? 1 : 0;
-        gbar(g);
+        gbar<GT>(g);
         return;
     }
     uint32_t prefix = 0, pmask = 0;
     int rem = m;
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int b = t; b < 256; b += G_NT) hist[b] = 0;
-        gbar(g);
+        for (int b = t; b < 256; b += GT) hist[b] = 0;
+        gbar<GT>(g);
         // warp-aggregated histogram: lanes holding the same digit add once
         for (int j = 0; j < chunk; ++j) {
             const int i = i0 + j;
@@ -673,7 +686,7 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
             const unsigned peers = __match_any_sync(0xffffffffu, bin);
             if (bin >= 0 && (t & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
         }
-        gbar(g);
+        gbar<GT>(g);
         if (t < 32) {
             int c[8], sum = 0;
 #pragma unroll
@@ -696,16 +709,16 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
                 }
             }
         }
-        gbar(g);
+        gbar<GT>(g);
         prefix |= ((uint32_t)sc.bin) << shift;
         pmask |= 255u << shift;
         rem = sc.remaining;
-        gbar(g);
+        gbar<GT>(g);
     }
     int eq = 0;
     for (int i = i0; i < i1; ++i) eq += (valid[i] && key[i] == prefix) ? 1 : 0;
     int tot;
-    int before = gscan_excl(eq, sc.red, g, t, &tot);
+    int before = gscan_excl<GT>(eq, sc.red, g, t, &tot);
     for (int i = i0; i < i1; ++i) {
         uint8_t s = 0;
         if (valid[i]) {
@@ -715,7 +728,7 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
         }
         sel[i] = s;
     }
-    gbar(g);
+    gbar<GT>(g);
 }
 
 // The two selections of a restore-swap round in one pass sequence: selA =
@@ -725,18 +738,19 @@ __device__ void group_select_top_m(const uint32_t *key, const uint8_t *valid, in
 // histB in `aux`, 2 x 256 + 2 ints of caller memory that is dead at this
 // point), and both sets share the element passes and the barriers; the two
 // radix scans run on the group's two warps side by side.
+template <int GT>
 __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop, int n, int mA, int mB,
                                         uint8_t *selA, uint8_t *selB, GroupScratch &sc, int *aux, int g, int t) {
     int *histA = aux, *histB = aux + 256;
     int *resB = aux + 512;  // bin, remaining of set B
-    const int chunk = (n + G_NT - 1) / G_NT;
+    const int chunk = (n + GT - 1) / GT;
     const int i0 = t * chunk, i1 = min(n, i0 + chunk);
     int nvA = 0, nvB = 0;
     for (int i = i0; i < i1; ++i) {
         if (drop[i]) ++nvA;
         else ++nvB;
     }
-    const int nv = gsum(nvA | (nvB << 16), sc.red, g, t);  // n < 2^16: the two counts do not mix
+    const int nv = gsum<GT>(nvA | (nvB << 16), sc.red, g, t);  // n < 2^16: the two counts do not mix
     const int n_validA = nv & 0xFFFF, n_validB = nv >> 16;
     if (mA < 0) mA = 0;
     if (mB < 0) mB = 0;
@@ -745,11 +759,11 @@ __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop
     int remA = mA, remB = mB;
     if (!(doneA && doneB)) {
         for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int b = t; b < 256; b += G_NT) {
+            for (int b = t; b < 256; b += GT) {
                 histA[b] = 0;
                 histB[b] = 0;
             }
-            gbar(g);
+            gbar<GT>(g);
             for (int j = 0; j < chunk; ++j) {
                 const int i = i0 + j;
                 int bin = -1;
@@ -765,10 +779,10 @@ __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop
                 if (bin >= 0 && (t & 31) == __ffs(peers) - 1)
                     atomicAdd(bin < 256 ? &histA[bin] : &histB[bin - 256], __popc(peers));
             }
-            gbar(g);
+            gbar<GT>(g);
             // warp 0 scans set A, warp 1 set B
             const int w = t >> 5, l = t & 31;
-            const bool active = w == 0 ? !doneA : !doneB;
+            const bool active = w == 0 ? !doneA : (w == 1 ? !doneB : false);
             if (active) {
                 const int *hist = w == 0 ? histA : histB;
                 const int rem = w == 0 ? remA : remB;
@@ -801,7 +815,7 @@ __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop
                     }
                 }
             }
-            gbar(g);
+            gbar<GT>(g);
             if (!doneA) {
                 prefA |= ((uint32_t)sc.bin) << shift;
                 remA = sc.remaining;
@@ -811,7 +825,7 @@ __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop
                 remB = resB[1];
             }
             pmask |= 255u << shift;
-            gbar(g);
+            gbar<GT>(g);
         }
     }
     int eqA = 0, eqB = 0;
@@ -821,7 +835,7 @@ __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop
         else eqB += (!doneB && k == prefB) ? 1 : 0;
     }
     int tot;
-    const int bef = gscan_excl(eqA | (eqB << 16), sc.red, g, t, &tot);
+    const int bef = gscan_excl<GT>(eqA | (eqB << 16), sc.red, g, t, &tot);
     int beforeA = bef & 0xFFFF, beforeB = bef >> 16;
     for (int i = i0; i < i1; ++i) {
         uint8_t a = 0, b = 0;
@@ -838,7 +852,7 @@ __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop
         selA[i] = a;
         selB[i] = b;
     }
-    gbar(g);
+    gbar<GT>(g);
 }
 
 // g, Mg, G, K, J of the current drop set, for one group.  The chains run
@@ -846,22 +860,24 @@ __device__ void group_select_top_m_dual(const uint32_t *key, const uint8_t *drop
 // starts at +0 is left bit-for-bit unchanged by adding a +0 or -0 product in
 // round-to-nearest, so this equals the sparse sum over the dropped entries
 // (the oracle's order) while letting the loads pipeline.
+template <int GT>
 __device__ void g_drift(GroupScratch &S, const float *P, float *Pd, const uint8_t *drop, const uint16_t *vbT,
                         int vstride, const float *Mt, int n_cand, int g, int t) {
-    for (int k = t; k < n_cand; k += G_NT) Pd[k] = drop[k] ? P[k] : 0.0f;
-    gbar(g);
-    float sp;
-    const float acc = col_chain(Pd, vbT + (size_t)t * vstride, n_cand, t == 0, sp);
+    for (int k = t; k < n_cand; k += GT) Pd[k] = drop[k] ? P[k] : 0.0f;
+    gbar<GT>(g);
+    float sp = 0.0f, acc = 0.0f;
+    if (t < HD) acc = col_chain(Pd, vbT + (size_t)t * vstride, n_cand, t == 0, sp);  // one chain per dimension
     if (t == 0) S.sum_pd = bf16r(sp);
-    gbar(g);
-    const float gd = __fsub_rn(__fmul_rn(S.sum_pd, S.vq[t]), bf16r(acc));
-    S.g[t] = gd;
-    gbar(g);
-    float mg = 0.0f;
+    gbar<GT>(g);
+    if (t < HD) S.g[t] = __fsub_rn(__fmul_rn(S.sum_pd, S.vq[t]), bf16r(acc));
+    gbar<GT>(g);
+    if (t < HD) {
+        float mg = 0.0f;
 #pragma unroll 16
-    for (int j = 0; j < HD; ++j) mg = __fmaf_rn(Mt[j * HD + t], S.g[j], mg);
-    S.Mg[t] = mg;
-    gbar(g);
+        for (int j = 0; j < HD; ++j) mg = __fmaf_rn(Mt[j * HD + t], S.g[j], mg);
+        S.Mg[t] = mg;
+    }
+    gbar<GT>(g);
     if (t == 0) {
         float G = 0.0f;
         for (int i = 0; i < HD; ++i) G = __fadd_rn(G, __fmul_rn(S.g[i], S.Mg[i]));
@@ -869,11 +885,11 @@ __device__ void g_drift(GroupScratch &S, const float *P, float *Pd, const uint8_
         S.K = clamp_min(__fsub_rn(S.tm, S.sum_pd), 1e-6f);
         S.J = __fdiv_rn(G, __fmul_rn(S.K, S.K));
     }
-    gbar(g);
+    gbar<GT>(g);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
+template <typename T, int GT>
+__global__ void __launch_bounds__(GT == 64 ? 8 * 64 : 5 * 128, 1) restore_swap_v2_kernel(
     const T *__restrict__ attn, const uint16_t *__restrict__ vb16, const float *__restrict__ tk,
     const float *__restrict__ Mg_in, const int32_t *__restrict__ nts, int H, int nq, int nkp, int n_cand,
     int rows_per_cta, int n_iters, Fracs fr, int track_best, uint8_t *__restrict__ drop_out,
@@ -905,7 +921,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
         for (int i = threadIdx.x; i < HD * HD; i += blockDim.x) M[(i & (HD - 1)) * HD + (i >> 6)] = Mg_in[(size_t)h * HD * HD + i];
     }
     __syncthreads();
-    const int g = threadIdx.x / G_NT, t = threadIdx.x % G_NT;
+    const int g = threadIdx.x / GT, t = threadIdx.x % GT;
     const int q = q0 + g;
     if (q >= nq) return;
     const int row = bh * nq + q;
@@ -923,28 +939,28 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
     uint8_t *sel = valid + n_cand;
     uint8_t *sel2 = sel + n_cand;
 
-    for (int k = t; k < nkp; k += G_NT) P[k] = bf16r(DT<T>::load(attn, (size_t)row * nkp + k));
-    gbar(g);
-    {
+    for (int k = t; k < nkp; k += GT) P[k] = bf16r(DT<T>::load(attn, (size_t)row * nkp + k));
+    gbar<GT>(g);
+    if (t < HD) {
         float s;
         const float acc = col_chain(P, vbT + (size_t)t * vstride, nkp, t == 0, s);
         S.vq[t] = bf16r(acc);
         if (t == 0) S.tm = bf16r(s);
     }
-    gbar(g);
-    {
+    gbar<GT>(g);
+    if (t < HD) {
         float acc = 0.0f;
 #pragma unroll 8
         for (int j = 0; j < HD; ++j) acc = __fmaf_rn(bf16r(M[j * HD + t]), S.vq[j], acc);
         S.Mvq[t] = bf16r(acc);
     }
-    gbar(g);
+    gbar<GT>(g);
     if (t == 0) {
         float s = 0.0f;
         for (int i = 0; i < HD; ++i) s = __fadd_rn(s, bf16r(__fmul_rn(S.Mvq[i], S.vq[i])));
         S.tqs = bf16r(s);
     }
-    gbar(g);
+    gbar<GT>(g);
     const float eps4 = bf16r(1e-4f);
     auto cut = [&](int k, float acc) {
         const float cross = bf16r(acc);
@@ -960,27 +976,27 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
         valid[k] = 1;
     };
     // four adjacent candidates per thread and step: four FMA chains, two per packed instruction
-    for (int k0 = 4 * t; k0 < n_cand; k0 += 4 * G_NT) {
+    for (int k0 = 4 * t; k0 < n_cand; k0 += 4 * GT) {
         float a[4];
         quad_chains(vbT, vstride, k0, S.Mvq, a);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             if (k0 + i < n_cand) cut(k0 + i, a[i]);
     }
-    gbar(g);
+    gbar<GT>(g);
     const int nt = nts[row];
-    group_select_top_m(key, valid, n_cand, min(nt, n_cand), sel, S, hist, g, t);
-    for (int k = t; k < n_cand; k += G_NT) drop[k] = sel[k] ? 0 : 1;
-    gbar(g);
+    group_select_top_m<GT>(key, valid, n_cand, min(nt, n_cand), sel, S, hist, g, t);
+    for (int k = t; k < n_cand; k += GT) drop[k] = sel[k] ? 0 : 1;
+    gbar<GT>(g);
     if (track_best) {
-        g_drift(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
+        g_drift<GT>(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
         if (t == 0) S.bestJ = S.J;
-        for (int k = t; k < n_cand; k += G_NT) best[k] = drop[k];
-        gbar(g);
+        for (int k = t; k < n_cand; k += GT) best[k] = drop[k];
+        gbar<GT>(g);
     }
     for (int it = 0; it < n_iters; ++it) {
         const int pic = (int)rintf(__fmul_rn(fr.f[it], (float)nt));
-        g_drift(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
+        g_drift<GT>(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
         if (t == 0) {
             S.flag = (track_best && S.J < S.bestJ) ? 1 : 0;
             if (S.flag) S.bestJ = S.J;
@@ -988,10 +1004,10 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
             for (int d = 0; d < HD; ++d) tq = __fadd_rn(tq, __fmul_rn(S.vq[d], S.Mg[d]));
             S.tqb = bf16r(tq);
         }
-        S.Mgb[t] = bf16r(S.Mg[t]);
-        gbar(g);
+        if (t < HD) S.Mgb[t] = bf16r(S.Mg[t]);
+        gbar<GT>(g);
         if (S.flag)
-            for (int k = t; k < n_cand; k += G_NT) best[k] = drop[k];
+            for (int k = t; k < n_cand; k += GT) best[k] = drop[k];
         const float G = S.G, K = S.K, tqb = S.tqb;
         int nd = 0, nk = 0, ben = 0;
         auto quality = [&](int k, float acc) {
@@ -1007,41 +1023,41 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
                 ++nk;
             }
         };
-        for (int k0 = 4 * t; k0 < n_cand; k0 += 4 * G_NT) {
+        for (int k0 = 4 * t; k0 < n_cand; k0 += 4 * GT) {
             float a[4];
             quad_chains(vbT, vstride, k0, S.Mgb, a);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 if (k0 + i < n_cand) quality(k0 + i, a[i]);
         }
-        const int n_drop = gsum(nd, S.red, g, t);
-        const int n_kept = gsum(nk, S.red, g, t);
-        const int beneficial = gsum(ben, S.red, g, t) > 0;
+        const int n_drop = gsum<GT>(nd, S.red, g, t);
+        const int n_kept = gsum<GT>(nk, S.red, g, t);
+        const int beneficial = gsum<GT>(ben, S.red, g, t) > 0;
         int cnt = pic;
         if (beneficial && cnt < 1) cnt = 1;
         cnt = min(cnt, n_drop);
         cnt = min(cnt, n_kept);
         if (!beneficial) cnt = 0;
-        group_select_top_m_dual(key, drop, n_cand, cnt, cnt, sel, sel2, S, hist, g, t);
-        for (int k = t; k < n_cand; k += G_NT) drop[k] = (uint8_t)((drop[k] && !sel[k]) || sel2[k]);
-        gbar(g);
+        group_select_top_m_dual<GT>(key, drop, n_cand, cnt, cnt, sel, sel2, S, hist, g, t);
+        for (int k = t; k < n_cand; k += GT) drop[k] = (uint8_t)((drop[k] && !sel[k]) || sel2[k]);
+        gbar<GT>(g);
     }
     if (track_best) {
-        g_drift(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
+        g_drift<GT>(S, P, Pd, drop, vbT, vstride, M, n_cand, g, t);
         if (!(S.J < S.bestJ))
-            for (int k = t; k < n_cand; k += G_NT) drop[k] = best[k];
-        gbar(g);
+            for (int k = t; k < n_cand; k += GT) drop[k] = best[k];
+        gbar<GT>(g);
     }
     if (drop_out)
-        for (int k = t; k < n_cand; k += G_NT) drop_out[(size_t)row * n_cand + k] = drop[k];
+        for (int k = t; k < n_cand; k += GT) drop_out[(size_t)row * n_cand + k] = drop[k];
     if (counts) {
         // keep list: ascending kept candidates (or leading sinks), then the sink blocks
-        const int chunk = (n_cand + G_NT - 1) / G_NT;
+        const int chunk = (n_cand + GT - 1) / GT;
         const int i0 = t * chunk, i1 = min(n_cand, i0 + chunk);
         int c = 0;
         for (int i = i0; i < i1; ++i) c += (!drop[i] || i < lead) ? 1 : 0;
         int tot;
-        int pos = gscan_excl(c, S.red, g, t, &tot);
+        int pos = gscan_excl<GT>(c, S.red, g, t, &tot);
         int32_t *list = lists ? lists + (size_t)row * list_width : nullptr;
         if (list) {
             for (int i = i0; i < i1; ++i)
@@ -1049,7 +1065,7 @@ __global__ void __launch_bounds__(8 * G_NT, 1) restore_swap_v2_kernel(
                     if (pos < list_width) list[pos] = i;
                     ++pos;
                 }
-            for (int j = t; j < sink_blocks; j += G_NT)
+            for (int j = t; j < sink_blocks; j += GT)
                 if (tot + j < list_width) list[tot + j] = n_cand + j;
         }
         if (t == 0) {
@@ -1124,16 +1140,23 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
         cudaGetDevice(&dev);
         if (dev >= 0 && dev < 64 && n_sm[dev] == 0) cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev);
         const int sms = (dev >= 0 && dev < 64 && n_sm[dev] > 0) ? n_sm[dev] : 148;
-        if (R >= 2 && (long long)BH * ((nq + R - 1) / R) < sms)
+        // With that few rows each SM holds few warps and a row's latency sets
+        // the time: rows then get 128-thread groups (per-candidate passes and
+        // selections spread over twice the threads; the drift chains stay on
+        // the first 64, one per dimension), at most 5 rows per CTA.
+        bool wide = false;
+        if (R >= 2 && (long long)BH * ((nq + R - 1) / R) < sms) {
             while (R > 2 && (long long)BH * ((nq + R - 2) / (R - 1)) <= sms) --R;
+            wide = R <= 5;
+        }
         if (R >= 2) {
             const size_t sm2 = fixed + (size_t)R * rowb;
-            auto k2 = restore_swap_v2_kernel<T>;
+            auto k2 = wide ? restore_swap_v2_kernel<T, 128> : restore_swap_v2_kernel<T, 64>;
             set_smem_attr((const void *)k2, sm2);
             const int ctas = BH * ((nq + R - 1) / R);
-            k2<<<ctas, R * G_NT, sm2, st>>>((const T *)attn_full, vb16, tk, M, nts, H, nq, nkp, n_cand, R, n_iters, fr,
-                                           track_best, drop, s, lists, counts, list_width, sink_blocks, lead, status,
-                                           rowb);
+            k2<<<ctas, R * (wide ? 128 : 64), sm2, st>>>((const T *)attn_full, vb16, tk, M, nts, H, nq, nkp, n_cand,
+                                                          R, n_iters, fr, track_best, drop, s, lists, counts,
+                                                          list_width, sink_blocks, lead, status, rowb);
             return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
         }
     }
