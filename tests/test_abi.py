@@ -55,6 +55,12 @@ def test_workspace_size():
     lambda L: L.ress_map_to_lists(None, 4, 10, None, None, 10, None, None),
     lambda L: L.ress_sparse_attn(None, None, None, None, None, 1, 128, 64, None, None, 1, 0.125, None, 0, 0,
                                  128, 0, None, None),
+    lambda L: L.ress_sparse_attn_sched(None, None, None, None, None, 1, 128, 64, None, None, 1, 0.125, None, 0, 0,
+                                       128, 0, None, None, None),
+    lambda L: L.ress_sparse_attn_split(None, None, None, None, None, 1, 128, 64, None, None, 1, 0.125, None, 0, 0,
+                                       128, 0, None, None, 0, None, None, None),
+    lambda L: L.ress_qkv_prologue(None, 1, 1, 16, 4, None, None, None, None, 1e-5, None, None, None, 0, None, None,
+                                  None, None),
 ])
 def test_bad_arguments_are_rejected_on_the_host(call):
     assert call(_lib.load()) == -1  # RESS_E_ARG
