@@ -1010,18 +1010,20 @@ __global__ void __launch_bounds__(GT == 64 ? 8 * 64 : 5 * 128, 1) restore_swap_v
             for (int k = t; k < n_cand; k += GT) best[k] = drop[k];
         const float G = S.G, K = S.K, tqb = S.tqb;
         int nd = 0, nk = 0, ben = 0;
+        // dropped and kept candidates differ only in the arguments of
+        // knorm_quality: select them and call it once (a quad of candidates
+        // mixes both, and a branch would run both sides in every warp)
         auto quality = [&](int k, float acc) {
             const float tkk = bf16r(acc);
             const float r = bf16r(__fmul_rn(P[k], bf16r(__fsub_rn(tkk, tqb))));
-            if (drop[k]) {
-                const float rq = knorm_quality(G, K, __fadd_rn(__fmul_rn(2.0f, r), bf16_from_bits(ssq[k])), P[k]);
-                key[k] = order_key(rq);
-                ben |= (rq > 0.0f) ? 1 : 0;
-                ++nd;
-            } else {
-                key[k] = order_key(knorm_quality(G, K, __fsub_rn(bf16_from_bits(ssq[k]), __fmul_rn(2.0f, r)), -P[k]));
-                ++nk;
-            }
+            const bool dk = drop[k] != 0;
+            const float sk = bf16_from_bits(ssq[k]), r2 = __fmul_rn(2.0f, r);
+            const float dG = dk ? __fadd_rn(r2, sk) : __fsub_rn(sk, r2);
+            const float rq = knorm_quality(G, K, dG, dk ? P[k] : -P[k]);
+            key[k] = order_key(rq);
+            ben |= (dk && rq > 0.0f) ? 1 : 0;
+            nd += dk ? 1 : 0;
+            nk += dk ? 0 : 1;
         };
         for (int k0 = 4 * t; k0 < n_cand; k0 += 4 * GT) {
             float a[4];
