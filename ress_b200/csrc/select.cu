@@ -369,17 +369,15 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
             float tkk = bf16r(acc);
             const float pk = bf16_from_bits(P[k]), sk = bf16_from_bits(ssq[k]);
             float r = bf16r(__fmul_rn(pk, bf16r(__fsub_rn(tkk, tqb))));
-            if (drop[k]) {
-                float rq = knorm_quality(G, K, __fadd_rn(__fmul_rn(2.0f, r), sk), pk);
-                key[k] = order_key(rq);
-                ben |= (rq > 0.0f) ? 1 : 0;
-                ++nd;
-            } else {
-                float cq = knorm_quality(G, K, __fsub_rn(sk, __fmul_rn(2.0f, r)), -pk);
-                key[k] = order_key(cq);
-                ++nk;
-            }
-            valid[k] = drop[k] ? 0 : 1;
+            // one knorm_quality call on selected arguments (no divergent branch)
+            const bool dk = drop[k] != 0;
+            const float r2 = __fmul_rn(2.0f, r);
+            const float rq = knorm_quality(G, K, dk ? __fadd_rn(r2, sk) : __fsub_rn(sk, r2), dk ? pk : -pk);
+            key[k] = order_key(rq);
+            ben |= (dk && rq > 0.0f) ? 1 : 0;
+            nd += dk ? 1 : 0;
+            nk += dk ? 0 : 1;
+            valid[k] = dk ? 0 : 1;
         }
         const int n_drop = block_sum_int<SEL_NT>(nd, S.sc.red);
         const int n_kept = block_sum_int<SEL_NT>(nk, S.sc.red);
