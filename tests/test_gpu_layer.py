@@ -248,3 +248,25 @@ def test_da3_shape_layer_matches_oracle():
     for i in range(o["counts"].numel()):
         c = int(o["counts"][i])
         assert torch.equal(lists[i, :c], o["lists"][i, :c]), i
+
+
+@pytest.mark.parametrize("attn_split", [None, 16])
+def test_layer_attn_split_option(attn_split):
+    """global_layer's attn_split option (the split attention launch for layers
+    with few rows: None lets the launch decide, and a 4-frame layer's 16 x 43
+    rows are few enough on a B200 to split its long rows; 16 forces 16-block
+    pieces): the keep lists are those of the default launch, and the outputs
+    agree with it within 2e-3 max abs."""
+    shape = synth.LayerShape(n_frames=4)
+    q, k, v = (t.cuda() for t in _data(shape, torch.bfloat16))
+    M = synth.metric_from_weight(synth.out_proj_weight()).cuda()
+    hs = synth.fisher_table(seed=1)[0, 3]
+    L = K.Layout(1, 16, shape.n_frames, shape.n_special, shape.hw)
+    budget = LY.BudgetSpec("hess", sparse_ratio=0.5, scores_norm=K.scores_norm(hs).cuda())
+    order = LY.OrderSpec("restore_swap", M=M)
+    ref = LY.global_layer(q, k, v, L, budget, order)
+    res = LY.global_layer(q, k, v, L, budget, order, attn_split=attn_split)
+    torch.cuda.synchronize()
+    K.check_status()
+    assert torch.equal(res.counts, ref.counts)
+    assert (res.out - ref.out).abs().max().item() < 2e-3
