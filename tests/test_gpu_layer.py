@@ -183,6 +183,29 @@ def test_cuda_graph_replay_equals_eager():
         assert torch.equal(r.counts, eager.counts)
 
 
+def test_cuda_graph_replay_with_split_attention():
+    """The same with the split attention launch (attn_split=16: scratch
+    allocated and the per-row counters zeroed inside the capture): replays
+    give the eager call's bits, twice in a row."""
+    shape, dtype = synth.LayerShape(n_frames=6), torch.bfloat16
+    q, k, v = (t.cuda() for t in _data(shape, dtype))
+    dev = q.device
+    M = synth.metric_from_weight(synth.out_proj_weight()).to(dev)
+    sn = K.scores_norm(synth.fisher_table(seed=1)[0, 1]).to(dev)
+    budget = LY.BudgetSpec("hess", sparse_ratio=0.5, scores_norm=sn)
+    L = K.Layout(1, 16, shape.n_frames, shape.n_special, shape.hw)
+    order = LY.OrderSpec("restore_swap", M=M)
+    eager = LY.global_layer(q, k, v, L, budget, order, attn_split=16)
+    out = torch.empty_like(eager.out)
+    cap = LY.CapturedLayer(lambda: LY.global_layer(q, k, v, L, budget, order, out=out, attn_split=16))
+    for _ in range(2):
+        r = cap.replay()
+        torch.cuda.synchronize()
+        K.check_status(dev)
+        assert torch.equal(r.out, eager.out)
+        assert torch.equal(r.counts, eager.counts)
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_view_sharded_layer_equals_full(world):
     """Frames sharded over `world` ranks, emulated in one process (the
