@@ -63,33 +63,50 @@ __device__ void emit_list(const uint8_t *keep, int n_cand, int lead, int sink_bl
 // Per head: bf16 copy of vbar and quadratic_deviation's term_k =
 // bf16(sum_i bf16(Mvk_i * v_i)), Mvk = bf16(M_bf16 v) (projected.py:283-285);
 // for the streamed restore-swap kernel also the transposed bf16 copy
-// vbT[bh][d][k] (row stride vt_stride).
+// vbT[bh][d][k] (row stride vt_stride).  One warp per pooled block k: lane l
+// runs the FMA chains of Mvk_l and Mvk_{l+32} (each over j in order), and
+// every lane then forms the sum over i in order from shuffled products.
+constexpr int VT_NT = 256, VT_K_PER_WARP = 4;
 template <typename T>
-__global__ void vbar_terms_kernel(const T *__restrict__ vbar, const float *__restrict__ M, int H,
-                                  int nkp, int n_cand, uint16_t *__restrict__ vb16,
-                                  float *__restrict__ tk, uint16_t *__restrict__ vbT, int vt_stride) {
-    __shared__ float Mb[HD * HD];
+__global__ void __launch_bounds__(VT_NT) vbar_terms_kernel(const T *__restrict__ vbar, const float *__restrict__ M,
+                                                           int H, int nkp, int n_cand, uint16_t *__restrict__ vb16,
+                                                           float *__restrict__ tk, uint16_t *__restrict__ vbT,
+                                                           int vt_stride) {
+    __shared__ float MbT[HD * HD];  // MbT[j * 64 + i] = bf16(M[i][j])
     const int bh = blockIdx.y, h = bh % H;
-    for (int i = threadIdx.x; i < HD * HD; i += blockDim.x) Mb[i] = bf16r(M[(size_t)h * HD * HD + i]);
+    for (int i = threadIdx.x; i < HD * HD; i += VT_NT) MbT[(i & (HD - 1)) * HD + (i >> 6)] = bf16r(M[(size_t)h * HD * HD + i]);
     __syncthreads();
-    const int k = blockIdx.x * blockDim.x + threadIdx.x;
-    if (k >= nkp) return;
-    float v[HD];
+    const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
+    const int k0 = (blockIdx.x * (VT_NT / 32) + warp) * VT_K_PER_WARP;
+    for (int k = k0; k < min(k0 + VT_K_PER_WARP, nkp); ++k) {
+        const size_t rowo = ((size_t)bh * nkp + k) * HD;
+        const float v0 = bf16r(DT<T>::load(vbar, rowo + 2 * l)), v1 = bf16r(DT<T>::load(vbar, rowo + 2 * l + 1));
+        vb16[rowo + 2 * l] = bf16bits(v0);
+        vb16[rowo + 2 * l + 1] = bf16bits(v1);
+        if (vbT != nullptr) {
+            vbT[((size_t)bh * HD + 2 * l) * vt_stride + k] = bf16bits(v0);
+            vbT[((size_t)bh * HD + 2 * l + 1) * vt_stride + k] = bf16bits(v1);
+        }
+        if (k >= n_cand) continue;
+        float a0 = 0.0f, a1 = 0.0f;  // Mvk_l, Mvk_{l+32}
 #pragma unroll
-    for (int j = 0; j < HD; ++j) {
-        v[j] = bf16r(DT<T>::load(vbar, ((size_t)bh * nkp + k) * HD + j));
-        vb16[((size_t)bh * nkp + k) * HD + j] = bf16bits(v[j]);
-        if (vbT != nullptr) vbT[((size_t)bh * HD + j) * vt_stride + k] = bf16bits(v[j]);
-    }
-    if (k >= n_cand) return;
-    float s = 0.0f;
-    for (int i = 0; i < HD; ++i) {
-        float acc = 0.0f;
+        for (int j = 0; j < HD; ++j) {
+            const float vj = __shfl_sync(0xffffffffu, (j & 1) ? v1 : v0, j >> 1);
+            a0 = __fmaf_rn(MbT[j * HD + l], vj, a0);
+            a1 = __fmaf_rn(MbT[j * HD + l + 32], vj, a1);
+        }
+        // v_l and v_{l+32} (held by lanes l/2 and 16 + l/2)
+        const float e0 = __shfl_sync(0xffffffffu, v0, l >> 1), o0 = __shfl_sync(0xffffffffu, v1, l >> 1);
+        const float e1 = __shfl_sync(0xffffffffu, v0, 16 + (l >> 1)), o1 = __shfl_sync(0xffffffffu, v1, 16 + (l >> 1));
+        const float p0 = bf16r(__fmul_rn(bf16r(a0), (l & 1) ? o0 : e0));
+        const float p1 = bf16r(__fmul_rn(bf16r(a1), (l & 1) ? o1 : e1));
+        float sum = 0.0f;
 #pragma unroll
-        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(Mb[i * HD + j], v[j], acc);
-        s = __fadd_rn(s, bf16r(__fmul_rn(bf16r(acc), v[i])));
+        for (int i = 0; i < 32; ++i) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, p0, i));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, p1, i));
+        if (l == 0) tk[(size_t)bh * n_cand + k] = bf16r(sum);
     }
-    tk[(size_t)bh * n_cand + k] = bf16r(s);
 }
 
 // ----------------------------------------------------------------- restore-swap
@@ -1121,8 +1138,9 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
     uint16_t *vbT = v2 ? nullptr
                        : reinterpret_cast<uint16_t *>(reinterpret_cast<char *>(ws) +
                                                       align256(off + (size_t)BH * n_cand * sizeof(float)));
-    vbar_terms_kernel<T><<<dim3((nkp + 127) / 128, BH), 128, 0, st>>>((const T *)vbar, M, H, nkp, n_cand,
-                                                                       vb16, tk, vbT, vt_stride);
+    constexpr int k_per_cta = (VT_NT / 32) * VT_K_PER_WARP;
+    vbar_terms_kernel<T><<<dim3((nkp + k_per_cta - 1) / k_per_cta, BH), VT_NT, 0, st>>>(
+        (const T *)vbar, M, H, nkp, n_cand, vb16, tk, vbT, vt_stride);
     Fracs fr;
     for (int i = 0; i < MAX_ITERS; ++i) fr.f[i] = i < n_iters ? fracs[i] : 0.0f;
     {
