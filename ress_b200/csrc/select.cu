@@ -612,14 +612,19 @@ __device__ __forceinline__ float col_chain(const float *w, const uint16_t *col, 
 
 // Four FMA chains over the 64 dimensions for candidates k0..k0+3 (k0 a
 // multiple of 4): a[i] = sum_d vbT[d][k0 + i] * b[d] in d order.
+// (b 16-byte aligned: its 64 weights come four per load)
 __device__ __forceinline__ void quad_chains(const uint16_t *vbT, int vstride, int k0, const float *b, float (&a)[4]) {
     a[0] = a[1] = a[2] = a[3] = 0.0f;
-#pragma unroll 16
-    for (int d = 0; d < HD; ++d) {
-        const uint2 v = *reinterpret_cast<const uint2 *>(vbT + (size_t)d * vstride + k0);
-        const float bd = b[d];
-        fma2_chain_fwd(a[0], a[1], bfl(v.x), bfh(v.x), bd);
-        fma2_chain_fwd(a[2], a[3], bfl(v.y), bfh(v.y), bd);
+#pragma unroll 4
+    for (int d4 = 0; d4 < HD; d4 += 4) {
+        const float4 b4 = *reinterpret_cast<const float4 *>(b + d4);
+        const float bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const uint2 v = *reinterpret_cast<const uint2 *>(vbT + (size_t)(d4 + e) * vstride + k0);
+            fma2_chain_fwd(a[0], a[1], bfl(v.x), bfh(v.x), bw[e]);
+            fma2_chain_fwd(a[2], a[3], bfl(v.y), bfh(v.y), bw[e]);
+        }
     }
 }
 
@@ -629,7 +634,7 @@ __device__ __forceinline__ void gbar(int g) { asm volatile("bar.sync %0, %1;" ::
 
 struct GroupScratch {
     int red[4];
-    int bin, remaining;
+    int bin, remaining, pad_[2];  // the arrays below start 16-byte aligned (float4 reads)
     float vq[HD], Mvq[HD], g[HD], Mg[HD], Mgb[HD];
     float tm, sum_pd, G, K, J, bestJ, tqb, tqs;
     int flag;
