@@ -375,6 +375,18 @@ def _sm_count(dev) -> int:
 # keeps the last wave short.
 SPLIT_WAVES = 3
 SPLIT_MAX = 2  # pieces per row at most (attn.cu)
+SPLIT_MAX_WIDTH = 16384  # widest keep list the split launch takes (attn.cu ORDER_MAX_WIDTH: one sort bin per count)
+
+
+def split_piece(rows: int, list_width: int, sm_count: int, schedule: bool = True):
+    """sparse_attn's split=None decision: the piece size in key blocks for a
+    launch of ``rows`` rows with keep lists ``list_width`` wide on
+    ``sm_count`` SMs, or False for one CTA per row.  Only launches of fewer
+    than SPLIT_WAVES waves of CTAs (two per SM) split; a row longer than the
+    piece then runs as up to SPLIT_MAX pieces."""
+    if schedule and rows < SPLIT_WAVES * 2 * sm_count and list_width <= SPLIT_MAX_WIDTH:
+        return max(32, (list_width + SPLIT_MAX - 1) // SPLIT_MAX)
+    return False
 
 
 def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout=None, sm_scale=None,
@@ -384,9 +396,9 @@ def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout
     positions of a (B, H, frames*(special+hw), 64) tensor.
     split: False (default) runs one CTA per row, the same bits whatever the
     launch; None lets launches of few rows (under SPLIT_WAVES waves) run rows
-    longer than a quarter of the list width as up to four pieces on separate
-    CTAs (outputs within the attention tolerance of the unsplit launch); an
-    int forces that piece size."""
+    longer than half the list width as two pieces on separate CTAs (outputs
+    within the attention tolerance of the unsplit launch; split_piece
+    decides); an int forces that piece size."""
     _dev_ok(q8, k8, v16, lists, counts)
     BH, Tq, _ = q8.shape
     Tk = k8.shape[1]
@@ -408,8 +420,7 @@ def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout
     lw = lists.shape[-1]
     rows = counts.numel()
     if split is None:
-        few = schedule and rows < SPLIT_WAVES * 2 * _sm_count(dev) and lw <= 16384
-        split = max(32, (lw + SPLIT_MAX - 1) // SPLIT_MAX) if few else False
+        split = split_piece(rows, lw, _sm_count(dev), schedule)
     if split is not False:
         item_order = torch.empty(SPLIT_MAX * rows, dtype=torch.int32, device=dev)
         partial = torch.empty(rows * SPLIT_MAX * 128 * 68, dtype=torch.float32, device=dev)
