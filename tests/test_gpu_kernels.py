@@ -297,10 +297,11 @@ def test_sparse_attention_random_maps(density):
 
 @pytest.mark.parametrize("chunk", [8, 30])
 def test_split_rows_match_oracle_and_unsplit(chunk):
-    """ress_sparse_attn_split: rows longer than `chunk` key blocks run as up
-    to four pieces of their list on separate CTAs, merged by the piece that
-    finishes last.  Random keep lists with a ragged key tail (47 key blocks:
-    at chunk 8 most rows split into four pieces, at chunk 30 into two):
+    """ress_sparse_attn_split: rows longer than `chunk` key blocks run as two
+    pieces of their list (the kernel's limit) on separate CTAs, merged by the
+    piece that finishes last.  Random keep lists with a ragged key tail (47
+    key blocks, ~33 kept per row: at chunk 8 nearly every row splits, at
+    chunk 30 about half of them):
     sampled rows within 2e-2 max / 1e-3 mean abs of the fp64 oracle, every
     row within 2e-3 of the one-CTA-per-row launch, and a second call on the
     same scratch (the per-row counters must be left at zero) gives the same
