@@ -300,8 +300,8 @@ def test_split_rows_match_oracle_and_unsplit(chunk):
     """ress_sparse_attn_split: rows longer than `chunk` key blocks run as two
     pieces of their list (the kernel's limit) on separate CTAs, merged by the
     piece that finishes last.  Random keep lists with a ragged key tail (47
-    key blocks, ~33 kept per row: at chunk 8 nearly every row splits, at
-    chunk 30 about half of them):
+    key blocks, ~33 kept per row and one in five rows a single block: at
+    chunk 8 every longer row splits, at chunk 30 about four in five):
     sampled rows within 2e-2 max / 1e-3 mean abs of the fp64 oracle, every
     row within 2e-3 of the one-CTA-per-row launch, and a second call on the
     same scratch (the per-row counters must be left at zero) gives the same
