@@ -1,7 +1,8 @@
-"""The host-side decision of the split attention launch (kernels.split_piece,
-the split=None path of kernels.sparse_attn): which launches spread their
-longest rows over two CTAs, and with what piece size.  Pure host logic, no
-GPU: the kernel side is covered by tests/test_gpu_kernels.py."""
+"""Host-side launch planning, no GPU: the decision of the split attention
+launch (kernels.split_piece, the split=None path of kernels.sparse_attn:
+which launches spread their longest rows over two CTAs, and with what piece
+size), and the token and block counts kernels.Layout gives the benchmark
+configurations.  The kernel side is covered by tests/test_gpu_kernels.py."""
 
 import pytest
 
@@ -40,3 +41,16 @@ def test_no_row_needs_more_than_split_max_pieces():
         piece = K.split_piece(1, width, SMS)
         assert piece >= 32
         assert -(-width // piece) <= K.SPLIT_MAX
+
+
+@pytest.mark.parametrize("frames,Tp,Tk,nq,nkp,n_cand,nkb,sinks", [
+    (4, 5476, 5496, 43, 86, 85, 86, 1),              # config 1
+    (32, 43808, 43968, 343, 685, 684, 687, 3),       # configs 2 and 3
+    (200, 273800, 274800, 2140, 4279, 4278, 4294, 16),  # config 4
+])
+def test_layout_of_the_configs(frames, Tp, Tk, nq, nkp, n_cand, nkb, sinks):
+    """Token and block counts of the VGGT global layer (5 special tokens and
+    37 x 37 patches per frame; attention.py:446-491 for the candidate/sink
+    split) for the benchmark configurations."""
+    L = K.Layout(1, 16, frames, 5, 37 * 37)
+    assert (L.Tp, L.Tk, L.nq, L.nkp, L.n_cand, L.nkb, L.sink_blocks) == (Tp, Tk, nq, nkp, n_cand, nkb, sinks)
