@@ -130,6 +130,30 @@ def test_single_drop_objective_is_renormalised_cut():
         assert torch.allclose(J, (s / (1 - p[j])) ** 2)
 
 
+def test_projected_score_with_identity_metric_is_the_damage_score():
+    """With M = I the projected score p_j * sqrt(q.Mq - 2 q.Mk + k.Mk)
+    (projected.py:259-288, 359-388) is the head-space damage score
+    p_j * ||v_q - V_j|| -- the reduction the reference relies on for its
+    "damage_restore_swap*" criteria (attention.py:562-568).  Checked on the
+    oracle's per-candidate score s, which follows the reference's bf16
+    expanded form; the bounds allow for that form's bf16 roundings."""
+    import oracle
+
+    g = torch.Generator().manual_seed(3)
+    nq, nkp, n_cand = 6, 40, 39
+    P = torch.softmax(torch.randn(nq, nkp, generator=g, dtype=torch.float64) * 2, -1).to(torch.bfloat16)
+    vb = (torch.randn(1, nkp, 64, generator=g) * 0.5).to(torch.bfloat16)
+    nts = torch.full((nq,), 10, dtype=torch.int32)
+    _, s = oracle.restore_swap(P, vb, torch.eye(64).unsqueeze(0), nts, n_cand, n_iters=0, track_best=False)
+    Pd, V = P.double(), vb[0].double()
+    vq = Pd @ V
+    dmg = Pd[:, :n_cand] * (vq.unsqueeze(1) - V[:n_cand].unsqueeze(0)).norm(dim=-1)
+    scale = Pd[:, :n_cand] * (vq.norm(dim=-1, keepdim=True) + V[:n_cand].norm(dim=-1).unsqueeze(0))
+    err = (s.double() - dmg).abs()
+    assert float((err / scale).max()) < 0.02
+    assert float((err / dmg).median()) < 0.01
+
+
 @pytest.mark.parametrize("frames,special", [(4, 5), (32, 5), (12, 5), (6, 1)])
 def test_no_special_key_is_a_candidate(frames, special):
     """Candidate blocks hold patch keys only; every special key lies in a sink
