@@ -15,7 +15,6 @@ Only the defaults of the reference's import-time switches are supported
 
 from __future__ import annotations
 
-import math
 import os
 from dataclasses import dataclass
 
@@ -25,7 +24,7 @@ import torch.nn.functional as F
 from . import criterion as _criterion
 from . import kernels as K
 from .budget import compute_baseline_num_to_select  # noqa: F401  (re-exported, reference location)
-from .layer import BudgetSpec, OrderSpec, global_layer
+from .layer import OrderSpec, global_layer
 from .qkv import compute_qkv, get_patch_tokens, project_out
 
 KS_Q = 128
