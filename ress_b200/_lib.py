@@ -14,6 +14,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libress_sm100.so")
 
 RESS_OK = 0
+RESS_E_ARG = -1
+RESS_E_DTYPE = -2
+RESS_E_SHAPE = -3
+RESS_E_LAUNCH = -4
+RESS_E_NO_DEVICE = -5
 RESS_E_SCRATCH = -6
 NOALLOC_SCRATCH_BYTES = 4 << 20
 RESS_F32, RESS_BF16 = 0, 1

@@ -116,6 +116,11 @@ __device__ __forceinline__ float div_by(float x, float d, float r) {
 
 // Workspace bytes ress_restore_swap needs (select.cu).
 size_t rs_scratch_bytes(int BH, int nkp, int n_cand);
+// The host-side argument checks of ress_restore_swap, workspace aside
+// (select.cu): RESS_OK or the RESS_E_* code that call returns.
+int rs_check_args(const void *attn_full, const void *vbar, const float *M, const int32_t *nts, int B, int H,
+                  int nq, int nkp, int n_cand, int n_iters, const float *fracs, const int32_t *counts,
+                  const int32_t *lists, const int32_t *status, int list_width, int sink_blocks, int lead_blocks);
 
 // -------------------------------------------------------- invariant division
 // n / d for a divisor fixed per launch, by multiply-high (T. Granlund and

@@ -10,6 +10,8 @@
 //   fused_round._round_kernel     src/ress/scoring/fused_round.py:125-197
 //   build_block_mask              src/ress/models/attention.py:147-174
 // Operation order = oracle/ress_oracle.c (bit-identical outputs).
+#include <climits>
+
 #include "common.cuh"
 
 namespace ress {
@@ -1119,6 +1121,21 @@ static bool rs_uses_v2(int nkp, int n_cand) {
 }
 static int rs_vt_stride(int nkp) { return (nkp + 7) & ~7; }
 static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+int rs_check_args(const void *attn_full, const void *vbar, const float *M, const int32_t *nts, int B, int H,
+                  int nq, int nkp, int n_cand, int n_iters, const float *fracs, const int32_t *counts,
+                  const int32_t *lists, const int32_t *status, int list_width, int sink_blocks, int lead_blocks) {
+    if (!attn_full || !vbar || !M || !nts || B <= 0 || H <= 0 || nq <= 0 || nkp <= 0 || n_cand <= 0 ||
+        n_cand > nkp || n_iters < 0 || n_iters > MAX_ITERS || sink_blocks < 0 || lead_blocks < 0 ||
+        (n_iters > 0 && !fracs))
+        return RESS_E_ARG;
+    if (counts && (!status || list_width <= 0)) return RESS_E_ARG;
+    if (lists && !counts) return RESS_E_ARG;
+    if ((long long)B * H * nq > INT_MAX) return RESS_E_SHAPE;
+    if (rs_smem(nkp, n_cand) > 200 * 1024 && rs2_fixed_bytes(nkp) + 2 * rs2_row_bytes(nkp, n_cand) > 220 * 1024)
+        return RESS_E_SHAPE;
+    return RESS_OK;
+}
+
 // Workspace of ress_restore_swap: bf16 vbar (BH, nkp, 64), then fp32 term_k
 // (BH, n_cand), then -- streamed kernel only -- the transposed bf16 vbar
 // (BH, 64, vt_stride); each part 256-byte aligned.
@@ -1214,14 +1231,10 @@ extern "C" int ress_restore_swap(int dtype, const void *attn_full, const void *v
                                  uint16_t *s, int32_t *lists, int32_t *counts, int list_width,
                                  int sink_blocks, int lead_blocks, int32_t *status, void *workspace,
                                  ress_stream_t stream) {
-    if (!attn_full || !vbar || !M || !nts || !workspace || B <= 0 || H <= 0 || nq <= 0 || nkp <= 0 ||
-        n_cand <= 0 || n_cand > nkp || n_iters < 0 || n_iters > MAX_ITERS || sink_blocks < 0 ||
-        lead_blocks < 0 || (n_iters > 0 && !fracs))
-        return RESS_E_ARG;
-    if (counts && (!status || list_width <= 0)) return RESS_E_ARG;
-    if (lists && !counts) return RESS_E_ARG;
-    if (rs_smem(nkp, n_cand) > 200 * 1024 && rs2_fixed_bytes(nkp) + 2 * rs2_row_bytes(nkp, n_cand) > 220 * 1024)
-        return RESS_E_SHAPE;
+    if (!workspace) return RESS_E_ARG;
+    const int rc = ress::rs_check_args(attn_full, vbar, M, nts, B, H, nq, nkp, n_cand, n_iters, fracs, counts,
+                                       lists, status, list_width, sink_blocks, lead_blocks);
+    if (rc != RESS_OK) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     if (dtype == RESS_F32)
         return restore_swap_t<float>(attn_full, vbar, M, nts, B, H, nq, nkp, n_cand, n_iters, fracs,
