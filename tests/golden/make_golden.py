@@ -2,7 +2,9 @@
 
 Run only where the reference tree is available (it is not on the GPU box):
 
-    python tests/golden/make_golden.py /path/to/libary753-ReSS
+    python tests/golden/make_golden.py /path/to/libary753-ReSS [case ...]
+
+(naming cases regenerates only those).
 
 The reference's GPU-only dependency SpargeAttn (``spas_sage_attn``) is absent,
 so its four imported symbols are stubbed; none of them is on the part of the
@@ -90,8 +92,18 @@ def build_block_mask_stable(fill, pooled_score, num_to_select, sink_blocks, rank
     return fm
 
 
+def _store_map(x, as_bits):
+    """A pooled map for the fixture: fp32 values, or -- for the large layers --
+    the raw 16-bit patterns of a bf16 map (half the bytes)."""
+    if as_bits and x.dtype == torch.bfloat16:
+        return x.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return x.float().numpy()
+
+
 def reference_layer(A, PJ, fill, shape, dtype, mode, sparse_ratio, cdf, lam=0.5, layer=0,
-                    n_iters=5):
+                    n_iters=5, heads=None):
+    """One layer through the reference.  heads: store the pooled maps of
+    these heads only (large layers); budgets and block maps cover all heads."""
     from ress.budget.hess import HessBudget
 
     q, k, v = synth.layer_qkv(shape, seed=0, dtype=dtype)
@@ -112,6 +124,7 @@ def reference_layer(A, PJ, fill, shape, dtype, mode, sparse_ratio, cdf, lam=0.5,
     vbar_full = A.block_mean_value(vp)
     Tk = kp.shape[-2] + ks.shape[-2]
     sink_blocks = math.ceil(Tk / A.KBLK) - n_cand
+    base = A.compute_baseline_num_to_select(attn_cond, sparse_ratio, cdf)
     nts = hess.num_to_select(layer, attn_cond, sparse_ratio, cdf, 1.0)
     nts = nts.clamp(min=min(A.MIN_NUM_TO_SELECT, n_cand))
     rank_by = None
@@ -132,9 +145,12 @@ def reference_layer(A, PJ, fill, shape, dtype, mode, sparse_ratio, cdf, lam=0.5,
         cs_M=synth.checksum(M),
         cs_qbar=synth.checksum(pooled_q.to(dtype)), cs_kbar=synth.checksum(pooled_k.to(dtype)),
         cs_vbar=synth.checksum(vbar_full),
-        attn_full=attn_full.float().numpy(),
-        attn_cond=attn_cond.float().numpy(),
+        attn_full=_store_map(attn_full if heads is None else attn_full[:, heads], heads is not None),
+        attn_cond=_store_map(attn_cond if heads is None else attn_cond[:, heads], heads is not None),
+        heads=np.arange(shape.n_heads) if heads is None else np.asarray(heads),
+        cs_attn_full=synth.checksum(attn_full), cs_attn_cond=synth.checksum(attn_cond),
         head_scores=hess.head_scores[layer].numpy(),
+        baseline=base.int().numpy(),
         nts=nts.int().numpy(),
         final_map=np.packbits(final_map.numpy(), axis=-1),
         final_map_width=final_map.shape[-1],
@@ -185,18 +201,29 @@ def budget_kats(PJ):
 def main(ref_root: str):
     torch.set_num_threads(os.cpu_count() or 1)
     A, PJ, fill = _install_reference(ref_root)
+    # The cfg2 layer (32 frames, bf16, apply_hess sr .5 /
+    # cdf .97 and apply_ress sr .5, HeSS lambda .5) stores the pooled maps of
+    # two heads only -- the one with the largest HeSS score (capped at every
+    # candidate) and the one with the smallest -- to keep the fixture small;
+    # its budgets and block maps cover all 16 heads.
+    cfg2_heads = [9, 3]
     cases = {
-        "cfg1_ress": (synth.CONFIG1, torch.float32, "ress", 0.1, None),
-        "cfg1_ress_sr50": (synth.CONFIG1, torch.float32, "ress", 0.5, None),
-        "cfg1_hess_cdf": (synth.CONFIG1, torch.float32, "prob", 0.5, 0.97),
-        "bf16_6f_ress": (synth.LayerShape(n_frames=6), torch.bfloat16, "ress", 0.5, None),
-        "bf16_6f_hess_cdf": (synth.LayerShape(n_frames=6), torch.bfloat16, "prob", 0.5, 0.97),
+        "cfg1_ress": (synth.CONFIG1, torch.float32, "ress", 0.1, None, None),
+        "cfg1_ress_sr50": (synth.CONFIG1, torch.float32, "ress", 0.5, None, None),
+        "cfg1_hess_cdf": (synth.CONFIG1, torch.float32, "prob", 0.5, 0.97, None),
+        "bf16_6f_ress": (synth.LayerShape(n_frames=6), torch.bfloat16, "ress", 0.5, None, None),
+        "bf16_6f_hess_cdf": (synth.LayerShape(n_frames=6), torch.bfloat16, "prob", 0.5, 0.97, None),
+        "cfg2_ress": (synth.LayerShape(n_frames=32), torch.bfloat16, "ress", 0.5, None, cfg2_heads),
+        "cfg2_hess_cdf": (synth.LayerShape(n_frames=32), torch.bfloat16, "prob", 0.5, 0.97, cfg2_heads),
     }
-    pooled_keys = ("attn_full", "attn_cond", "head_scores", "cs_q", "cs_k", "cs_v", "cs_M",
-                   "cs_qbar", "cs_kbar", "cs_vbar")
+    only = set(sys.argv[2:])
+    pooled_keys = ("attn_full", "attn_cond", "head_scores", "heads", "cs_attn_full", "cs_attn_cond", "cs_q",
+                   "cs_k", "cs_v", "cs_M", "cs_qbar", "cs_kbar", "cs_vbar")
     written = set()
-    for name, (shape, dtype, mode, sr, cdf) in cases.items():
-        d = reference_layer(A, PJ, fill, shape, dtype, mode, sr, cdf)
+    for name, (shape, dtype, mode, sr, cdf, heads) in cases.items():
+        if only and name not in only:
+            continue
+        d = reference_layer(A, PJ, fill, shape, dtype, mode, sr, cdf, heads=heads)
         stem = name.split("_")[0] + "_" + name.split("_")[1] if name.startswith("bf16") else name.split("_")[0]
         if stem not in written:
             np.savez_compressed(os.path.join(HERE, f"{stem}_pooled.npz"),
@@ -206,11 +233,12 @@ def main(ref_root: str):
         case["pooled"] = stem
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **case)
         print("wrote", name, d["final_map"].shape)
-    np.savez_compressed(os.path.join(HERE, "budget_kats.npz"), **budget_kats(PJ))
-    print("wrote budget_kats")
+    if not only or "budget_kats" in only:
+        np.savez_compressed(os.path.join(HERE, "budget_kats.npz"), **budget_kats(PJ))
+        print("wrote budget_kats")
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: python tests/golden/make_golden.py <path of the reference tree>")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference tree> [case ...]")
     main(sys.argv[1])

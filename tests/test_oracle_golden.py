@@ -17,10 +17,11 @@ import oracle
 from ress_b200 import synth
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
-CASES = ["cfg1_ress", "cfg1_ress_sr50", "cfg1_hess_cdf", "bf16_6f_ress", "bf16_6f_hess_cdf"]
+CASES = ["cfg1_ress", "cfg1_ress_sr50", "cfg1_hess_cdf", "bf16_6f_ress", "bf16_6f_hess_cdf", "cfg2_ress",
+         "cfg2_hess_cdf"]
 # minimum fraction of (head, q-block) rows identical end to end
 E2E_FLOOR = {"cfg1_ress": 1.0, "cfg1_ress_sr50": 1.0, "cfg1_hess_cdf": 0.995,
-             "bf16_6f_ress": 0.995, "bf16_6f_hess_cdf": 0.995}
+             "bf16_6f_ress": 0.995, "bf16_6f_hess_cdf": 0.995, "cfg2_ress": 0.99, "cfg2_hess_cdf": 0.99}
 
 _inputs = {}
 
@@ -44,6 +45,14 @@ def _layer(case):
         q, k, v = synth.layer_qkv(shape, seed=0, dtype=dtype)
         _inputs[key] = (q, k, v)
     return shape, dtype, _inputs[key]
+
+
+def _pooled_map(pooled, key, dtype):
+    """A stored pooled map: fp32 values, or raw bf16 bit patterns (large layers)."""
+    a = pooled[key]
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
+    return torch.from_numpy(a).to(dtype)
 
 
 def _final_map(case):
@@ -81,31 +90,37 @@ def test_selection_bit_exact_given_reference_map(name):
     case, pooled = _load(name)
     shape, dtype, (q, k, v) = _layer(case)
     n_cand = int(case["n_cand"])
-    attn_full = torch.from_numpy(pooled["attn_full"]).to(dtype)
+    heads = torch.from_numpy(pooled["heads"]).long()  # heads whose pooled maps the fixture holds
+    attn_full = _pooled_map(pooled, "attn_full", dtype)
+    cond = _pooled_map(pooled, "attn_cond", dtype)
     fm_ref = _final_map(case)[0]
     nts_ref = torch.from_numpy(case["nts"])
     nh, nq = nts_ref.shape[1], nts_ref.shape[2]
-    # the budget, from the reference's attn_cond
-    cond = torch.from_numpy(pooled["attn_cond"]).to(dtype)
+    sub = len(heads)
+    # the budget: the baseline from the reference's attn_cond, then HeSS on the
+    # reference's baselines of every head (it couples the heads of a q-block)
     sr = float(case["sparse_ratio"])
     cdf = float(case["cdf"])
     base = oracle.baseline(cond, sr, None if cdf < 0 else cdf)
-    nts = oracle.hess_adjust(base.view(1, nh, nq), oracle.scores_norm(torch.from_numpy(pooled["head_scores"])),
+    base_ref = torch.from_numpy(case["baseline"])
+    assert torch.equal(base.view(1, sub, nq), base_ref[:, heads])
+    nts = oracle.hess_adjust(base_ref.view(1, nh, nq), oracle.scores_norm(torch.from_numpy(pooled["head_scores"])),
                              n_cand, min_clamp=min(2, n_cand))
     assert torch.equal(nts, nts_ref)
+    nts_sub = nts_ref[:, heads].reshape(-1)
     if str(case["mode"]) == "ress":
-        vp = synth.split_tokens(v, shape)[0]
-        vbar = oracle.pool_mean(vp.reshape(nh, -1, 64), 64).to(torch.bfloat16)
-        M = synth.metric_from_weight(synth.out_proj_weight(), nh)
-        drop, _ = oracle.restore_swap(attn_full, vbar, M, nts_ref.view(-1), n_cand)
+        vp = synth.split_tokens(v, shape)[0][:, heads]
+        vbar = oracle.pool_mean(vp.reshape(sub, -1, 64), 64).to(torch.bfloat16)
+        M = synth.metric_from_weight(synth.out_proj_weight(), nh)[heads]
+        drop, _ = oracle.restore_swap(attn_full, vbar, M, nts_sub, n_cand)
         keep = ~drop
     else:
-        keep = oracle.top_m_mask(cond.view(-1, n_cand), nts_ref.view(-1))
+        keep = oracle.top_m_mask(cond.reshape(-1, n_cand), nts_sub)
     lists, counts = oracle.keep_lists(keep, int(case["sink_blocks"]))
-    got = torch.zeros(nh * nq, fm_ref.shape[-1], dtype=torch.bool)
-    for r in range(nh * nq):
+    got = torch.zeros(sub * nq, fm_ref.shape[-1], dtype=torch.bool)
+    for r in range(sub * nq):
         got[r, lists[r, : counts[r]].long()] = True
-    assert torch.equal(got.view_as(fm_ref), fm_ref)
+    assert torch.equal(got.view(sub, nq, -1), fm_ref[heads])
 
 
 @pytest.mark.parametrize("name", CASES)
@@ -120,12 +135,14 @@ def test_end_to_end_agreement(name):
     o = oracle.layer_select(qp, kp, vp, ks.shape[-2], M, head_scores=torch.from_numpy(pooled["head_scores"]),
                             mode="ress" if str(case["mode"]) == "ress" else "prob",
                             sparse_ratio=float(case["sparse_ratio"]), cdf_threshold=None if cdf < 0 else cdf)
-    af_ref = torch.from_numpy(pooled["attn_full"])
-    af = o["attn_full"].float().view_as(af_ref)
+    heads = torch.from_numpy(pooled["heads"]).long()
+    af_ref = _pooled_map(pooled, "attn_full", dtype).float()
+    af = o["attn_full"].float().view(1, shape.n_heads, *af_ref.shape[-2:])[:, heads]
     rel = ((af - af_ref).abs() / af_ref.abs().clamp(min=1e-30)).max().item()
     assert rel < (1e-5 if dtype == torch.float32 else 1e-2)
     fm_ref = _final_map(case)[0, :, :, : o["n_cand"]]
     same = (o["keep"][0] == fm_ref).all(-1).float().mean().item()
+    print(f"{name}: {same:.5f} of (head, q-block) rows identical end to end")
     assert same >= E2E_FLOOR[name], f"{name}: {same:.4f} of rows identical"
 
 
