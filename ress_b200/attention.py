@@ -126,8 +126,9 @@ def _order_for(self, block_criterion, hd, nh, device):
         if spec.maximize or spec.invert_cut:
             raise NotImplementedError(f"{block_criterion!r}: drift-maximisation controls are not ported")
         if spec.use_wo:
-            assert getattr(self, "M", None) is not None, (
-                f"block_criterion={block_criterion!r} requires bake_and_attach_M(model) to have been called first")
+            if getattr(self, "M", None) is None:
+                raise AssertionError(f"{block_criterion!r} weighs drift by the output projection: attach the "
+                                     "per-head metrics with bake_and_attach_M(model) before the forward")
             M = self.M.float().to(device)
         else:
             M = torch.eye(hd, device=device, dtype=torch.float32).expand(nh, hd, hd).contiguous()

@@ -57,12 +57,13 @@ def get_backbone(name):
     try:
         return BACKBONES[name]
     except KeyError:
-        raise ValueError(f"unknown backbone {name!r} -- known: {', '.join(sorted(BACKBONES))}") from None
+        raise ValueError(f"no backbone is registered as {name!r}; the registry holds "
+                         f"{', '.join(sorted(BACKBONES))}") from None
 
 
 def infer_backbone(model):
     name = getattr(model, "_ress_backbone", None)
     if name is None:
-        raise ValueError("cannot tell which backbone this model is -- pass backbone=\"vggt\"/\"pi3\"/"
-                         "\"da3\" explicitly, or load it with load_backbone(), which tags it.")
+        raise ValueError("this model has no _ress_backbone tag: name its backbone with the backbone= "
+                         "argument, or create it with load_backbone(), which sets the tag")
     return get_backbone(name)

@@ -36,11 +36,12 @@ def fused_round_step(P, term_k, s_sq, term_q, drop_mask, per_iter_count, big_dty
                      kept_mass=None, knorm_dtype=None, k_eps=1e-6):
     """Returns (new_drop_mask bool, restore_count int64) like the reference."""
     knorm = knorm_dtype is not None
-    assert knorm == (g_norm_sq is not None) == (kept_mass is not None), (
-        "fused_round_step: g_norm_sq, kept_mass and knorm_dtype must be given together")
+    if not knorm == (g_norm_sq is not None) == (kept_mass is not None):
+        raise AssertionError("the kept-mass objective uses g_norm_sq, kept_mass and knorm_dtype together: "
+                             "pass all three or none")
     raw_dtype, q_dtype = _step_dtypes(P, term_k, s_sq, big_dtype, knorm_dtype)
     if P.dtype not in _SUPPORTED or s_sq.dtype not in _SUPPORTED:
-        raise TypeError("P/term_k/s_sq must be float32 or bfloat16")
+        raise TypeError("the round step takes float32 or bfloat16 P, term_k and s_sq only")
     new_drop, cnt = K.round_step(P, term_k.to(P.dtype), s_sq, term_q, drop_mask, per_iter_count,
                                  raw_bf16=raw_dtype is torch.bfloat16, q_bf16=q_dtype is torch.bfloat16,
                                  g_norm_sq=g_norm_sq, kept_mass=kept_mass, k_eps=k_eps)

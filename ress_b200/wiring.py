@@ -32,9 +32,9 @@ def wire_ress_attention(model, blocks, aux_output_store=None, aux_full=True, num
         store = aux_output_store[i] if aux_output_store is not None else None
 
         def _fwd(self, x, pos=None, xpos=None, attn_bias=None, attn_mask=None, _store=store, _attn=block.attn):
-            assert attn_bias is None and attn_mask is None, (
-                "ress_attention_forward builds its own block mask and cannot honor an "
-                "externally supplied attn_bias/attn_mask")
+            if attn_bias is not None or attn_mask is not None:
+                raise AssertionError("the sparse global attention decides which key blocks each query block "
+                                     "sees; a caller-side attn_bias or attn_mask has no place in it")
             return ress_attention_forward(
                 _attn, x, pos if pos is not None else xpos,
                 num_to_select=getattr(_attn, "num_to_select", None),
