@@ -9,32 +9,39 @@
 // non-causal, keys past Tk masked.  Q and K arrive as per-block int8 with
 // fp32 scales (ress_score_quant), V as fp16.
 //
-// One CTA per row, 7 warps:
+// One CTA per row, 12 warps in three warpgroups:
 //   warp 0      TMA producer: Q tile once, then K/V tiles of the listed
 //               blocks through an NS-stage ring (cp.async.bulk.tensor);
 //               also allocates / frees the CTA's tensor memory.
 //   warp 1      S issuer (one thread): S_j = Q K_j^T with tcgen05.mma
 //               kind::i8 into a TMEM double buffer.
-//   warps 2-5   softmax: thread = query row = TMEM lane.  Reads S_j with
-//               tcgen05.ld, keeps the running max, writes P_j (fp16) into
-//               an NP-deep ring of shared-memory tiles in the 128B-swizzled
-//               K-major layout the MMA reads.
-//   warp 6      P.V issuer (one thread): O += P_j V_j with kind::f16
+//   warp 2      P.V issuer (one thread): O += P_j V_j with kind::f16
 //               (fp16 x fp16 -> fp32 in TMEM).  The MMA has N = 80, the
 //               extra 16 B columns being ones, so O's columns 64..79 carry
 //               the softmax denominator sum(P) at no CUDA-core cost.
+//   warp 3      idle (completes warpgroup 0).
+//   warps 4-11  softmax, two threads per query row: warp w reads TMEM lane
+//               quarter w % 4 (warpgroup 1 its first 16 lanes, warpgroup 2
+//               the last 16) with the 16x32bx2 load shape, so lanes 0-15 of
+//               a warp hold key columns 0-31 of 16 rows and lanes 16-31
+//               columns 32-63 of the same rows; a row maximum is one shuffle.
+//               Each thread keeps the running max of its row and writes its
+//               half of P_j (fp16) into an NP-deep ring of shared-memory
+//               tiles in the 128B-swizzled K-major layout the MMA reads.
+// Two CTAs per SM: each SM sub-partition runs four softmax warps, which hide
+// each other's load, reduction and exp latencies.  The register file of a
+// sub-partition holds six warps at 80 registers; setmaxnreg moves registers
+// from warpgroup 0 (single-thread control loops) to the softmax warpgroups.
 // S and P.V are issued by different threads so that neither waits behind
 // the other: S_j is issued as soon as the softmax has read S_{j-2}, K_j has
 // landed and P.V_{j-NP} has completed (P_j reuses that P.V's shared tile, so
 // the softmax warps never wait for the tile themselves), P.V_j as soon as
 // P_j is written.  The softmax warps probe S_{j+1}'s barrier without
 // blocking before block j's exponentials and use the answer after them, so
-// a ready S costs no wait latency (measured: the two already-complete
-// barrier checks per block took ~400 of ~1,800 clocks).
+// a ready S costs no wait latency.
 // The softmax loop body holds only the full-block path; the first block,
 // a ragged last key block and the (rare) O rescale run out of line, which
-// keeps the hot loop small in the instruction cache (measured: the inline
-// general path cost ~8 % of the kernel time).
+// keeps the hot loop small in the instruction cache.
 // Every mbarrier wait is bounded (~2 s); on expiry the CTA raises an abort
 // flag, records RESS_STATUS_ATTN_WAIT_TIMEOUT, drains its own in-flight
 // copies and MMAs, frees its tensor memory and exits.
@@ -48,7 +55,16 @@
 namespace ress {
 namespace attn {
 
-constexpr int NT = 224;
+constexpr int NT = 384;                // three warpgroups
+constexpr int NSOFT = 256;             // softmax threads (warpgroups 1 and 2)
+constexpr int PV_WARP = 2;
+// Registers per thread after the warpgroups' setmaxnreg: warpgroup 0 (TMA
+// producer and MMA issuers) gives up registers the softmax warpgroups take.
+// The launch provides NT x 80 (two CTAs per SM); the split must not exceed
+// it: 128 x REGS_CTRL + 256 x REGS_SOFT <= 384 x 80.
+constexpr int REGS_CTRL = 32;
+constexpr int REGS_SOFT = 104;
+static_assert(128 * REGS_CTRL + 256 * REGS_SOFT <= NT * 80, "register split above the launch's registers");
 constexpr int NS = 4;                  // K/V ring stages
 constexpr int NP = 3;                  // P ring stages
 constexpr int Q_BYTES = 128 * 64;      // int8
@@ -64,7 +80,6 @@ constexpr int OFF_ONES = OFF_P + NP * P_BYTES;
 constexpr int SMEM_TILES = OFF_ONES + ONES_BYTES;
 constexpr int SMEM_BYTES = SMEM_TILES + 1024;  // + alignment slack
 constexpr uint32_t TMEM_COLS = 256;            // S[2] (64 each) + O (80), power of two
-constexpr int O_COLS = 80;                      // 64 output columns + 16 columns of sum(P)
 constexpr float RESCALE_THRESH = 8.0f;         // lazy rescale when the max grows by > 2^8
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
 
@@ -176,33 +191,49 @@ __device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
         "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
-// 16 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+// TMEM access with the 16x32bx2 shape: the warp covers 16 lanes (rows) from
+// the lane in taddr; lanes 0-15 of the warp read columns [col, col + n) of
+// those rows and lanes 16-31 columns [col + split, col + split + n).
+// Row halves: n = 32, split = 32 (columns 0-31 / 32-63 of a 64-column tile).
+__device__ __forceinline__ void tmem_ld_half32(uint32_t taddr, uint32_t *v) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *v) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32], 32;"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
           "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
           "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
         : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_st_half32(uint32_t taddr, const uint32_t *v) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "tcgen05.st.sync.aligned.16x32bx2.x32.b32 [%0], 32, {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
+// The 16 row-sum columns (64-79 of O): n = 8, split = 8.
+__device__ __forceinline__ void tmem_ld_half8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.16x32bx2.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], 8;"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st_half8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.16x32bx2.x8.b32 [%0], 8, {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+// One row-sum column: column 64 for lanes 0-15, column 72 for lanes 16-31
+// (every column 64-79 holds the same sum).
+__device__ __forceinline__ uint32_t tmem_ld_rowsum(uint32_t taddr) {
+    uint32_t v;
+    asm volatile("tcgen05.ld.sync.aligned.16x32bx2.x1.b32 {%0}, [%1], 8;" : "=r"(v) : "r"(taddr));
+    return v;
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float r;
@@ -256,45 +287,50 @@ constexpr uint32_t MAGIC_I = 0x4B400000u;
 
 // Per-thread softmax state handed to the out-of-line paths.
 struct RowCtx {
-    uint32_t tS, tO, lane_addr, sP, prow, rsw;
+    uint32_t tS, tO, lane_addr, sP, prow, rsw, ch0;
+    int col0;  // first key column of this thread's half row (0 or 32)
     uint64_t *o_full;
     volatile int *abort_flag;
     int32_t *status;
 };
 
-// Multiplies this thread's row of O (TMEM, 64 output + 16 row-sum columns)
-// by alpha.  Out of line: rescales are rare after the first few blocks.
+// Multiplies this thread's half of its row of O (TMEM: 32 of the 64 output
+// columns and 8 of the 16 row-sum columns) by alpha.  Out of line: rescales
+// are rare after the first few blocks.
 __device__ __noinline__ void rescale_o(uint32_t tO, uint32_t lane_addr, float alpha) {
-#pragma unroll 1
-    for (int ch = 0; ch < O_COLS / 16; ++ch) {
-        uint32_t o16[16];
-        tmem_ld16(tO + ch * 16 + lane_addr, o16);
-        tmem_wait_ld();
+    uint32_t o[32];
+    tmem_ld_half32(tO + lane_addr, o);
+    uint32_t s8[8];
+    tmem_ld_half8(tO + HD + lane_addr, s8);
+    tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 16; ++t) o16[t] = __float_as_uint(__uint_as_float(o16[t]) * alpha);
-        tmem_st16(tO + ch * 16 + lane_addr, o16);
-    }
+    for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) s8[t] = __float_as_uint(__uint_as_float(s8[t]) * alpha);
+    tmem_st_half32(tO + lane_addr, o);
+    tmem_st_half8(tO + HD + lane_addr, s8);
     tmem_wait_st();
 }
 
-// Writes P = 2^(c*s + bias) for the first nvalid columns (0 beyond) of this
-// thread's row into the P tile at pbase (fp16, 128B-swizzled K-major).
-__device__ __forceinline__ void store_p_masked(const uint32_t (&sv)[64], int nvalid, float c, float bias,
-                                               uint32_t pbase, uint32_t rsw) {
+// Writes P = 2^(c*s + bias) for this thread's 32 key columns (col0 + t, 0
+// where col0 + t >= nvalid) of its row into the P tile at pbase (fp16,
+// 128B-swizzled K-major; 16-byte chunks ch0..ch0+3 of the row).
+__device__ __forceinline__ void store_p_masked(const uint32_t (&sv)[32], int nvalid, int col0, float c, float bias,
+                                               uint32_t pbase, uint32_t rsw, uint32_t ch0) {
 #pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
+    for (int ch = 0; ch < 4; ++ch) {
         uint32_t h[4];
 #pragma unroll
         for (int t = 0; t < 8; t += 2) {
             const int i0 = ch * 8 + t;
             float x0, x1;
             fma2(x0, x1, __uint_as_float(sv[i0]), __uint_as_float(sv[i0 + 1]), c, bias);
-            x0 = i0 < nvalid ? x0 : -INFINITY;
-            x1 = i0 + 1 < nvalid ? x1 : -INFINITY;
+            x0 = col0 + i0 < nvalid ? x0 : -INFINITY;
+            x1 = col0 + i0 + 1 < nvalid ? x1 : -INFINITY;
             __half2 hp = __floats2half2_rn(ex2(x0), ex2(x1));
             h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
         }
-        const uint32_t a = pbase + (((uint32_t)ch ^ rsw) << 4);
+        const uint32_t a = pbase + (((ch0 + (uint32_t)ch) ^ rsw) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
                      : "memory");
     }
@@ -307,18 +343,18 @@ __device__ __forceinline__ void store_p_masked(const uint32_t (&sv)[64], int nva
 // Returns false when a bounded wait failed.
 __device__ __noinline__ bool softmax_block_general(const RowCtx &rc, int j, int sb, int pb, int nvalid, float c,
                                                    float &m, uint64_t *s_free) {
-    uint32_t sv[64];
-    tmem_ld32(rc.tS + sb * 64 + rc.lane_addr, sv);
-    tmem_ld32(rc.tS + sb * 64 + 32 + rc.lane_addr, sv + 32);
+    uint32_t sv[32];
+    tmem_ld_half32(rc.tS + sb * 64 + rc.lane_addr, sv);
     tmem_wait_ld();
     fence_before();
     mbar_arrive(s_free);
     float fmx = -INFINITY;
 #pragma unroll
-    for (int t = 0; t < 64; ++t) {
+    for (int t = 0; t < 32; ++t) {
         sv[t] += MAGIC_I;
-        if (t < nvalid) fmx = fmaxf(fmx, __uint_as_float(sv[t]));
+        if (rc.col0 + t < nvalid) fmx = fmaxf(fmx, __uint_as_float(sv[t]));
     }
+    fmx = fmaxf(fmx, __shfl_xor_sync(0xffffffffu, fmx, 16));  // the row's other half
     const float mx = c * (fmx - MAGIC_F);
     const bool grow = mx > m + RESCALE_THRESH;
     const float m_new = grow ? mx : m;
@@ -329,7 +365,7 @@ __device__ __noinline__ bool softmax_block_general(const RowCtx &rc, int j, int 
         rescale_o(rc.tO, rc.lane_addr, grow ? ex2(m - m_new) : 1.0f);
     }
     m = m_new;
-    store_p_masked(sv, nvalid, c, fmaf(-c, MAGIC_F, -m), rc.sP + pb * P_BYTES + rc.prow, rc.rsw);
+    store_p_masked(sv, nvalid, rc.col0, c, fmaf(-c, MAGIC_F, -m), rc.sP + pb * P_BYTES + rc.prow, rc.rsw, rc.ch0);
     fence_before();
     return true;
 }
@@ -421,10 +457,10 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&B.s_full[i], 1);
-            mbar_init(&B.s_free[i], 128);
+            mbar_init(&B.s_free[i], NSOFT);
         }
         for (int i = 0; i < NP; ++i) {
-            mbar_init(&B.p_full[i], 128);
+            mbar_init(&B.p_full[i], NSOFT);
             mbar_init(&B.o_full[i], 1);
         }
         mbar_init(&B.s_done, 1);
@@ -444,6 +480,12 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     const uint32_t tmem = B.tmem_base;
     const uint32_t tS = tmem, tO = tmem + 128;
 
+    // Registers are rebalanced at the top of each warpgroup's branch (and not
+    // before it, so that the compiler allocates each branch at its own count):
+    // warpgroup 0 runs single-thread control loops, the softmax warpgroups
+    // hold a half row of S and the row state.
+    if (warp < 4) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CTRL));
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0 && cnt > 0) {
@@ -502,7 +544,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             while (!mbar_try_wait(addr, 0) && globaltimer() - t0 < TIMEOUT_NS) {
             }
         }
-    } else if (warp == 6) {
+    } else if (warp == PV_WARP) {
         // ------------------------------------------------------------ P.V issuer
         if (lane == 0 && cnt > 0) {
             for (int j = 0; j < cnt; ++j) {
@@ -532,23 +574,29 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             while (!mbar_try_wait(addr, 0) && globaltimer() - t0 < TIMEOUT_NS) {
             }
         }
+    }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFT));
         // ------------------------------------------------------------ softmax
-        // thread = query row = TMEM lane.  S is read once into registers as
-        // float bits of (1.5 * 2^23 + s) (exact for |s| < 2^22; |s| <= 64 *
-        // 127^2), so the scale-and-subtract is one FMA per element.  O
-        // accumulates in TMEM across blocks; it is rescaled only when a row's
-        // maximum grows by more than 2^RESCALE_THRESH (P then stays <= 2^8,
-        // well inside fp16), after waiting for the previous P.V.
+        // Two threads per query row (see the file header): thread = (row r,
+        // key columns col0..col0+31).  S is read once into registers as float
+        // bits of (1.5 * 2^23 + s) (exact for |s| < 2^22; |s| <= 64 * 127^2),
+        // so the scale-and-subtract is one FMA per element.  O accumulates in
+        // TMEM across blocks; it is rescaled only when a row's maximum grows
+        // by more than 2^RESCALE_THRESH (P then stays <= 2^8, well inside
+        // fp16), after waiting for the previous P.V.
         const int quad = warp & 3;
-        const int r = quad * 32 + lane;
-        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const int lane0 = quad * 32 + ((warp >> 2) - 1) * 16;  // first TMEM lane (row) of this warp
+        const int r = lane0 + (lane & 15);
+        const int col0 = (lane >> 4) * 32;
+        const uint32_t lane_addr = (uint32_t)lane0 << 16;
         const float qs = qscale[(size_t)bh * nqb + qb];
         float m = -INFINITY;
         bool ok = true;
         const uint32_t prow = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
         const uint32_t rsw = (uint32_t)(r & 7);
-        const RowCtx rc{tS, tO, lane_addr, sP, prow, rsw, B.o_full, abort_flag, status};
+        const uint32_t ch0 = (uint32_t)(col0 >> 3);  // first 16-byte chunk of the half row
+        const RowCtx rc{tS, tO, lane_addr, sP, prow, rsw, ch0, col0, B.o_full, abort_flag, status};
         const float *ksc = kscale + (size_t)bh * nkb;
         // two-deep prefetch: block j+2's index and block j+1's scale are
         // loaded one iteration before they are needed
@@ -573,15 +621,14 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                 if (!softmax_block_general(rc, j, sb, pb, nvalid, c, m, &B.s_free[sb])) { ok = false; break; }
             } else {
                 // hot path: a full block after the first
-                uint32_t sv[64];
-                tmem_ld32(tS + sb * 64 + lane_addr, sv);
-                tmem_ld32(tS + sb * 64 + 32 + lane_addr, sv + 32);
+                uint32_t sv[32];
+                tmem_ld_half32(tS + sb * 64 + lane_addr, sv);
                 tmem_wait_ld();
                 fence_before();
                 mbar_arrive(&B.s_free[sb]);
                 float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-                for (int t = 0; t < 64; t += 8) {
+                for (int t = 0; t < 32; t += 8) {
 #pragma unroll
                     for (int u = 0; u < 8; ++u) sv[t + u] += MAGIC_I;
                     a0 = max3(a0, __uint_as_float(sv[t]), __uint_as_float(sv[t + 1]));
@@ -589,7 +636,9 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                     a2 = max3(a2, __uint_as_float(sv[t + 4]), __uint_as_float(sv[t + 5]));
                     a3 = max3(a3, __uint_as_float(sv[t + 6]), __uint_as_float(sv[t + 7]));
                 }
-                const float mx = c * (max3(a0, a1, fmaxf(a2, a3)) - MAGIC_F);
+                float fmx = max3(a0, a1, fmaxf(a2, a3));
+                fmx = fmaxf(fmx, __shfl_xor_sync(0xffffffffu, fmx, 16));  // the row's other half
+                const float mx = c * (fmx - MAGIC_F);
                 // lazy rescale: the maximum moves only when it grew by more than the threshold
                 const bool grow = mx > m + RESCALE_THRESH;
                 if (__any_sync(0xffffffffu, grow)) {
@@ -606,7 +655,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                 // probe S_{j+1} now; the answer is used after this block's exponentials
                 s_ready = mbar_test_wait(smem_u32(&B.s_full[sb ^ 1]), ((j + 1) >> 1) & 1);
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
+                for (int ch = 0; ch < 4; ++ch) {
                     uint32_t h[4];
 #pragma unroll
                     for (int t = 0; t < 8; t += 2) {
@@ -616,7 +665,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                         __half2 hp = __floats2half2_rn(ex2(x0), ex2(x1));
                         h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
                     }
-                    const uint32_t a = pbase + (((uint32_t)ch ^ rsw) << 4);
+                    const uint32_t a = pbase + (((ch0 + (uint32_t)ch) ^ rsw) << 4);
                     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]),
                                  "r"(h[3])
                                  : "memory");
@@ -641,64 +690,48 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         const int bh_e = row_e / nqb, qb_e = row_e - bh_e * nqb;
         const int t = qb_e * 128 + r;
         float l = 0.0f;  // sum(P) from the ones columns of O
+        uint32_t o[32];  // this thread's half row of O (unnormalised)
         if (ok && cnt > 0) {
-            uint32_t o16[16];
-            tmem_ld16(tO + 64 + lane_addr, o16);
+            const uint32_t lv = tmem_ld_rowsum(tO + HD + lane_addr);
+            tmem_ld_half32(tO + lane_addr, o);
             tmem_wait_ld();
-            l = __uint_as_float(o16[0]);
+            l = __uint_as_float(lv);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
         const long long tt = (long long)(t / out_hw) * (out_hw + out_special) + out_special + (t % out_hw);
-        float *dst = out + (size_t)bh_e * out_sh + tt * out_st;
+        float *dst = out + (size_t)bh_e * out_sh + tt * out_st + col0;
         const int pieces_e = split_launch ? split_pieces(max(min(__ldg(&counts[row_e]), list_width), 0), split_chunk) : 1;
         if (pieces_e == 1) {
             const float inv = (ok && cnt > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+            if (t < Tq) {
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t o16[16];
-                if (ok && cnt > 0) {
-                    tmem_ld16(tO + ch * 16 + lane_addr, o16);
-                    tmem_wait_ld();
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) o16[i] = 0u;
-                }
-                if (t < Tq) {
-#pragma unroll
-                    for (int i = 0; i < 16; i += 4)
-                        *reinterpret_cast<float4 *>(dst + ch * 16 + i) =
-                            make_float4(__uint_as_float(o16[i]) * inv, __uint_as_float(o16[i + 1]) * inv,
-                                        __uint_as_float(o16[i + 2]) * inv, __uint_as_float(o16[i + 3]) * inv);
-                }
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4 *>(dst + i) =
+                        make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                                    __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
             }
         } else {
             // this piece's partial (O unnormalised, m, l) for query r
             float *mine = partial + ((size_t)row_e * SPLIT_MAX + piece_e) * PART_SLOT + (size_t)r * PART_ROW;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t o16[16];
-                if (ok) {
-                    tmem_ld16(tO + ch * 16 + lane_addr, o16);
-                    tmem_wait_ld();
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) o16[i] = 0u;
-                }
-#pragma unroll
-                for (int i = 0; i < 16; i += 4)
-                    *reinterpret_cast<float4 *>(mine + ch * 16 + i) =
-                        make_float4(__uint_as_float(o16[i]), __uint_as_float(o16[i + 1]), __uint_as_float(o16[i + 2]),
-                                    __uint_as_float(o16[i + 3]));
+            for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4 *>(mine + col0 + i) =
+                    make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]),
+                                __uint_as_float(o[i + 3]));
+            if (col0 == 0) {
+                mine[HD] = m;
+                mine[HD + 1] = ok ? l : 0.0f;
             }
-            mine[HD] = m;
-            mine[HD + 1] = ok ? l : 0.0f;
             __threadfence();
-            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
-            if (r == 0) {
+            asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps
+            if (r == 0 && col0 == 0) {
                 const int prev = atomicAdd(&row_done[row_e], 1);
                 B.merge = prev == pieces_e - 1;
                 if (prev == pieces_e - 1) row_done[row_e] = 0;  // every piece in: ready for the next launch
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync 1, 256;" ::: "memory");
             if (B.merge) {
                 // the last piece to finish merges all of them, in piece order
                 __threadfence();
@@ -722,12 +755,13 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                 const float inv = (ok && lsum > 0.0f) ? 1.0f / lsum : 0.0f;
                 if (t < Tq) {
 #pragma unroll
-                    for (int i = 0; i < HD; i += 4) {
+                    for (int i = 0; i < 32; i += 4) {
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                         for (int p = 0; p < SPLIT_MAX; ++p) {
                             if (p < pieces_e) {
-                                const float4 ov = __ldcg(reinterpret_cast<const float4 *>(base + p * PART_SLOT + i));
+                                const float4 ov =
+                                    __ldcg(reinterpret_cast<const float4 *>(base + p * PART_SLOT + col0 + i));
                                 acc.x = fmaf(ov.x, w[p], acc.x);
                                 acc.y = fmaf(ov.y, w[p], acc.y);
                                 acc.z = fmaf(ov.z, w[p], acc.z);
