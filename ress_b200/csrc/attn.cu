@@ -41,7 +41,9 @@
 // a ready S costs no wait latency.
 // The softmax loop body holds only the full-block path; the first block,
 // a ragged last key block and the (rare) O rescale run out of line, which
-// keeps the hot loop small in the instruction cache.
+// keeps the hot loop small in the instruction cache.  Lists are ascending,
+// so a ragged key block (the one holding key Tk - 1) can only be a row's
+// last entry; the loop runs over the blocks between the first and it.
 // Every mbarrier wait is bounded (~2 s); on expiry the CTA raises an abort
 // flag, records RESS_STATUS_ATTN_WAIT_TIMEOUT, drains its own in-flight
 // copies and MMAs, frees its tensor memory and exits.
@@ -341,8 +343,8 @@ __device__ __forceinline__ void store_p_masked(const uint32_t (&sv)[32], int nva
 // TMEM buffer sb itself (the caller has waited for it) and releases it.
 // Out of line so that the hot loop holds only the full-block path.
 // Returns false when a bounded wait failed.
-__device__ __noinline__ bool softmax_block_general(const RowCtx &rc, int j, int sb, int pb, int nvalid, float c,
-                                                   float &m, uint64_t *s_free) {
+__device__ __noinline__ float softmax_block_general(const RowCtx &rc, int j, int sb, int pb, int nvalid, float c,
+                                                    float m, uint64_t *s_free) {
     uint32_t sv[32];
     tmem_ld_half32(rc.tS + sb * 64 + rc.lane_addr, sv);
     tmem_wait_ld();
@@ -360,14 +362,13 @@ __device__ __noinline__ bool softmax_block_general(const RowCtx &rc, int j, int 
     const float m_new = grow ? mx : m;
     if (__any_sync(0xffffffffu, grow && j > 0)) {
         const int pj = j - 1;
-        if (!wait_bar_warp(&rc.o_full[pj % NP], (pj / NP) & 1, rc.abort_flag, rc.status)) return false;
+        if (!wait_bar_warp(&rc.o_full[pj % NP], (pj / NP) & 1, rc.abort_flag, rc.status)) return __int_as_float(0x7fffffff);
         fence_after();
         rescale_o(rc.tO, rc.lane_addr, grow ? ex2(m - m_new) : 1.0f);
     }
-    m = m_new;
-    store_p_masked(sv, nvalid, rc.col0, c, fmaf(-c, MAGIC_F, -m), rc.sP + pb * P_BYTES + rc.prow, rc.rsw, rc.ch0);
+    store_p_masked(sv, nvalid, rc.col0, c, fmaf(-c, MAGIC_F, -m_new), rc.sP + pb * P_BYTES + rc.prow, rc.rsw, rc.ch0);
     fence_before();
-    return true;
+    return m_new;
 }
 
 struct Bars {
@@ -598,83 +599,113 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         const uint32_t ch0 = (uint32_t)(col0 >> 3);  // first 16-byte chunk of the half row
         const RowCtx rc{tS, tO, lane_addr, sP, prow, rsw, ch0, col0, B.o_full, abort_flag, status};
         const float *ksc = kscale + (size_t)bh * nkb;
+
+        // block 0 and a ragged last block (keys past Tk) take the general path;
+        // blocks [1, hot_end) are full blocks after the first
+        const int kb_last = cnt > 0 ? lst[cnt - 1] : 0;
+        const int hot_end = (cnt > 1 && Tk - kb_last * 64 < 64) ? cnt - 1 : cnt;
+        if (cnt > 0) {
+            const int kb0 = lst[0];
+            const float c0 = qs * ksc[kb0] * sm_scale_log2;
+            if (!wait_bar_warp(&B.s_full[0], 0, abort_flag, status)) ok = false;
+            fence_after();
+            if (ok) {
+                m = softmax_block_general(rc, 0, 0, 0, min(64, Tk - kb0 * 64), c0, m, &B.s_free[0]);
+                ok = m == m;  // NaN: a bounded wait failed
+            }
+            if (ok) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&B.p_full[0]);
+            }
+        }
         // two-deep prefetch: block j+2's index and block j+1's scale are
         // loaded one iteration before they are needed
-        int kb_cur = cnt > 0 ? lst[0] : 0;
-        int kb_nxt = cnt > 1 ? lst[1] : 0;
-        float ks_cur = cnt > 0 ? ksc[kb_cur] : 0.0f;
+        int kb_nxt = cnt > 2 ? lst[2] : 0;
+        float ks_cur = cnt > 1 ? ksc[lst[1]] : 0.0f;
         bool s_ready = false;  // S_j's phase already seen complete by an early probe
-        for (int j = 0; j < cnt; ++j) {
-            const int sb = j & 1, pb = j % NP;
-            const int kb = kb_cur;
+        int pb = 1 % NP;
+        // swizzled offsets of this thread's four 16-byte chunks in its P row
+        uint32_t poff[4];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) poff[ch] = prow + (((ch0 + (uint32_t)ch) ^ rsw) << 4);
+        int j = 1;
+        for (; ok && j < hot_end; ++j) {
+            const int sb = j & 1;
             const float c = qs * ks_cur * sm_scale_log2;
             ks_cur = (j + 1 < cnt) ? ksc[kb_nxt] : 0.0f;
-            kb_cur = kb_nxt;
             kb_nxt = (j + 2 < cnt) ? lst[j + 2] : 0;
-            const int nvalid = min(64, Tk - kb * 64);
             if (!__all_sync(0xffffffffu, s_ready) && !wait_bar_warp(&B.s_full[sb], (j >> 1) & 1, abort_flag, status)) {
                 ok = false;
                 break;
             }
             fence_after();
-            if (j == 0 || nvalid < 64) {
-                if (!softmax_block_general(rc, j, sb, pb, nvalid, c, m, &B.s_free[sb])) { ok = false; break; }
-            } else {
-                // hot path: a full block after the first
-                uint32_t sv[32];
-                tmem_ld_half32(tS + sb * 64 + lane_addr, sv);
-                tmem_wait_ld();
-                fence_before();
-                mbar_arrive(&B.s_free[sb]);
-                float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+            uint32_t sv[32];
+            tmem_ld_half32(tS + sb * 64 + lane_addr, sv);
+            tmem_wait_ld();
+            fence_before();
+            mbar_arrive(&B.s_free[sb]);
 #pragma unroll
-                for (int t = 0; t < 32; t += 8) {
+            for (int u = 0; u < 32; ++u) sv[u] += MAGIC_I;
+            float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) sv[t + u] += MAGIC_I;
-                    a0 = max3(a0, __uint_as_float(sv[t]), __uint_as_float(sv[t + 1]));
-                    a1 = max3(a1, __uint_as_float(sv[t + 2]), __uint_as_float(sv[t + 3]));
-                    a2 = max3(a2, __uint_as_float(sv[t + 4]), __uint_as_float(sv[t + 5]));
-                    a3 = max3(a3, __uint_as_float(sv[t + 6]), __uint_as_float(sv[t + 7]));
-                }
-                float fmx = max3(a0, a1, fmaxf(a2, a3));
-                fmx = fmaxf(fmx, __shfl_xor_sync(0xffffffffu, fmx, 16));  // the row's other half
-                const float mx = c * (fmx - MAGIC_F);
-                // lazy rescale: the maximum moves only when it grew by more than the threshold
-                const bool grow = mx > m + RESCALE_THRESH;
-                if (__any_sync(0xffffffffu, grow)) {
-                    const float m_new = grow ? mx : m;
-                    const int pj = j - 1;
-                    if (!wait_bar_warp(&B.o_full[pj % NP], (pj / NP) & 1, abort_flag, status)) { ok = false; break; }
-                    fence_after();
-                    rescale_o(tO, lane_addr, ex2(m - m_new));
-                    m = m_new;
-                }
-                // P_{j-NP} (same tile) was consumed: S_j is issued only after its P.V completed
-                const uint32_t pbase = sP + pb * P_BYTES + prow;
-                const float bias = fmaf(-c, MAGIC_F, -m);
-                // probe S_{j+1} now; the answer is used after this block's exponentials
-                s_ready = mbar_test_wait(smem_u32(&B.s_full[sb ^ 1]), ((j + 1) >> 1) & 1);
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    uint32_t h[4];
-#pragma unroll
-                    for (int t = 0; t < 8; t += 2) {
-                        const int i0 = ch * 8 + t;
-                        float x0, x1;
-                        fma2(x0, x1, __uint_as_float(sv[i0]), __uint_as_float(sv[i0 + 1]), c, bias);
-                        __half2 hp = __floats2half2_rn(ex2(x0), ex2(x1));
-                        h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
-                    }
-                    const uint32_t a = pbase + (((ch0 + (uint32_t)ch) ^ rsw) << 4);
-                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]),
-                                 "r"(h[3])
-                                 : "memory");
-                }
-                fence_before();
+            for (int t = 0; t < 32; t += 8) {
+                a0 = max3(a0, __uint_as_float(sv[t]), __uint_as_float(sv[t + 1]));
+                a1 = max3(a1, __uint_as_float(sv[t + 2]), __uint_as_float(sv[t + 3]));
+                a2 = max3(a2, __uint_as_float(sv[t + 4]), __uint_as_float(sv[t + 5]));
+                a3 = max3(a3, __uint_as_float(sv[t + 6]), __uint_as_float(sv[t + 7]));
             }
+            float fmx = max3(a0, a1, fmaxf(a2, a3));
+            fmx = fmaxf(fmx, __shfl_xor_sync(0xffffffffu, fmx, 16));  // the row's other half
+            const float mx = c * (fmx - MAGIC_F);
+            // lazy rescale: the maximum moves only when it grew by more than the threshold
+            const bool grow = mx > m + RESCALE_THRESH;
+            if (__any_sync(0xffffffffu, grow)) {
+                const float m_new = grow ? mx : m;
+                const int pj = j - 1;
+                if (!wait_bar_warp(&B.o_full[pj % NP], (pj / NP) & 1, abort_flag, status)) { ok = false; break; }
+                fence_after();
+                rescale_o(tO, lane_addr, ex2(m - m_new));
+                m = m_new;
+            }
+            // P_{j-NP} (same tile) was consumed: S_j is issued only after its P.V completed
+            const float bias = fmaf(-c, MAGIC_F, -m);
+            // probe S_{j+1} now; the answer is used after this block's exponentials
+            s_ready = mbar_test_wait(smem_u32(&B.s_full[sb ^ 1]), ((j + 1) >> 1) & 1);
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t h[4];
+#pragma unroll
+                for (int t = 0; t < 8; t += 2) {
+                    const int i0 = ch * 8 + t;
+                    float x0, x1;
+                    fma2(x0, x1, __uint_as_float(sv[i0]), __uint_as_float(sv[i0 + 1]), c, bias);
+                    __half2 hp = __floats2half2_rn(ex2(x0), ex2(x1));
+                    h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
+                }
+                const uint32_t a = sP + pb * P_BYTES + poff[ch];
+                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]),
+                             "r"(h[3])
+                             : "memory");
+            }
+            fence_before();
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&B.p_full[pb]);
-            if (j == 0 || nvalid < 64) s_ready = false;
+            pb = pb == NP - 1 ? 0 : pb + 1;
+        }
+        if (ok && hot_end < cnt) {
+            // the ragged last block
+            const int sb = j & 1;
+            const float c = qs * ks_cur * sm_scale_log2;
+            if (!wait_bar_warp(&B.s_full[sb], (j >> 1) & 1, abort_flag, status)) ok = false;
+            fence_after();
+            if (ok) {
+                m = softmax_block_general(rc, j, sb, j % NP, Tk - kb_last * 64, c, m, &B.s_free[sb]);
+                ok = m == m;
+            }
+            if (ok) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&B.p_full[j % NP]);
+            }
         }
         if (ok && cnt > 0) {
             ok = wait_bar_warp(&B.o_full[(cnt - 1) % NP], ((cnt - 1) / NP) & 1, abort_flag, status);
