@@ -172,6 +172,30 @@ def _setup(frames, world, rank, device):
                 order_prob=order_prob, shard=shard, h0=h0, hl=hl, heads=heads)
 
 
+def _int8_peak(device):
+    """Dense int8 tensor-core throughput (TOP/s) of this GPU: cuBLASLt int8 x
+    int8 -> int32 GEMM at 8192^3 through torch._int_mm, best of 10 CUDA-event
+    timed calls after 3 warm-ups (the int8 counterpart of the driver's bf16
+    burst figure)."""
+    n = 8192
+    g = torch.Generator(device=device).manual_seed(0)
+    a = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=device, generator=g)
+    b = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=device, generator=g)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = None
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    del a, b
+    return 2.0 * n ** 3 / (best / 1e3) / 1e12
+
+
 def _attn_flops(lists, counts, L):
     """Kept-block FLOPs: 4 * q_rows * k_rows * 64 per (row, kept block)."""
     rows = counts.numel()
@@ -196,64 +220,113 @@ def _time_region(fn, steps, stream):
     return start.elapsed_time(end)
 
 
-def _cpu_baseline(S, samples_attn=8):
-    """The oracle (C, OpenMP over all host threads) on one cfg2 layer:
-    scoring + budget + restore-swap on the full layer, attention on a sample
-    of q-block rows extrapolated to the layer."""
+def _cpu_layer_once(S, t):
+    """One cfg2 layer on the host cores: the oracle's scoring + HeSS +
+    restore-swap selection (C, OpenMP) and fp32 block-gathered attention over
+    every (head, q-block) row.  Fills t["select"], t["attn"] (seconds)."""
     import oracle
+
+    q, k, v, qp, key, val, M, hs = S["_cpu"]
+    t0 = time.perf_counter()
+    o = oracle.layer_select(qp, key[..., : qp.shape[-2], :], val[..., : qp.shape[-2], :], key.shape[-2] - qp.shape[-2],
+                            M, head_scores=hs, mode="ress", sparse_ratio=SPARSE_RATIO)
+    t1 = time.perf_counter()
+    oracle.gathered_attention_fp32(qp, key, val, o["lists"], o["counts"])
+    t2 = time.perf_counter()
+    t["select"], t["attn"] = t1 - t0, t2 - t1
+    return o
+
+
+def _cpu_prepare(S):
     from ress_b200 import synth
 
-    shape = S["shape"]
-    q, k, v = (t.cpu() for t in (S["q"], S["k"], S["v"]))
-    qp, _ = synth.split_tokens(q, shape)
-    kp, ks = synth.split_tokens(k, shape)
-    vp, vs = synth.split_tokens(v, shape)
-    M = S["order"].M.cpu()
-    hs = S["budget"].scores_norm.cpu()
-    t0 = time.perf_counter()
-    o = oracle.layer_select(qp, kp, vp, ks.shape[-2], M, head_scores=hs, mode="ress", sparse_ratio=SPARSE_RATIO)
-    key = torch.cat([kp, ks], dim=-2)
-    val = torch.cat([vp, vs], dim=-2)
-    q8, qs, k8, ksc, km = oracle.quantize_qk(qp, key)
-    t1 = time.perf_counter()
-    H = qp.shape[1]
-    nq = o["nts"].shape[-1]
-    g = torch.Generator().manual_seed(0)
-    samp = [(int(torch.randint(0, H, (1,), generator=g)), int(torch.randint(0, nq, (1,), generator=g)))
-            for _ in range(samples_attn)]
-    v16 = val.reshape(H, -1, 64).to(torch.float16)
-    t2 = time.perf_counter()
-    oracle.sparse_attn_rows(q8, qs, k8, ksc, v16, o["lists"].view(H, nq, -1), o["counts"].view(H, nq), samp)
-    t3 = time.perf_counter()
-    per_layer = (t1 - t0) + (t3 - t2) * (H * nq) / samples_attn
-    return {"value": shape.n_frames / per_layer, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-            "sample": (f"oracle scoring+quant+HeSS+restore-swap on the full cfg2 layer ({t1 - t0:.2f} s) + fp64 "
-                       f"attention on {samples_attn} of {H * nq} (head, q-block) rows ({t3 - t2:.2f} s), "
-                       f"extrapolated to one layer ({per_layer:.1f} s)")}
+    if "_cpu" not in S:
+        shape = S["shape"]
+        q, k, v = (t.cpu() for t in (S["q"], S["k"], S["v"]))
+        qp, _ = synth.split_tokens(q, shape)
+        kp, ks = synth.split_tokens(k, shape)
+        vp, vs = synth.split_tokens(v, shape)
+        S["_cpu"] = (q, k, v, qp, torch.cat([kp, ks], -2), torch.cat([vp, vs], -2), S["order"].M.cpu(),
+                     S["budget"].scores_norm.cpu())
+    return S["_cpu"]
+
+
+def _cpu_baseline(S, reps=3):
+    """The path on the host cores over one whole cfg2 layer (no extrapolation):
+    selection by the oracle, attention as fp32 block-gathered torch matmuls
+    over every (head, q-block) row and its kept blocks.  One warm-up layer,
+    then the median of `reps` timed layers; the two legs are reported
+    separately."""
+    import oracle
+
+    _cpu_prepare(S)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    runs = []
+    for i in range(reps + 1):
+        t = {}
+        _cpu_layer_once(S, t)
+        if i > 0:
+            runs.append(t)
+    runs.sort(key=lambda t: t["select"] + t["attn"])
+    med = runs[len(runs) // 2]
+    per_layer = med["select"] + med["attn"]
+    return {"value": S["shape"].n_frames / per_layer, "unit": UNIT, "cores": threads, "kind": "port",
+            "select_s": round(med["select"], 4), "attn_s": round(med["attn"], 4),
+            "cpu": _cpu_model(), "oracle_threads": oracle.num_threads(), "torch_threads": torch.get_num_threads(),
+            "sample": (f"one whole cfg2 layer per run, median of {reps} after one warm-up: oracle scoring + "
+                       f"HeSS + restore-swap ({med['select']:.2f} s) and fp32 block-gathered torch attention "
+                       f"over all {S['L'].H * S['L'].nq} (head, q-block) rows ({med['attn']:.2f} s)")}
+
+
+def _cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 def run_reference(args):
-    """--impl reference: the CPU path of the reference restated in the oracle,
-    on the host cores; rank 0 only."""
+    """--impl reference: the path on the host cores (the oracle's selection
+    and fp32 block-gathered attention, see _cpu_baseline), one whole cfg2
+    layer per step; rank 0 only."""
     ws, rank, local = _dist()
     if rank != 0:
         return
     device = "cuda" if torch.cuda.is_available() else "cpu"
     S = _setup(args.frames, 1, 0, device)
-    steps = max(1, min(args.steps, 2))
-    vals = []
-    cb = None
-    for i in range(min(args.warmup, 1) + steps):
-        cb = _cpu_baseline(S, samples_attn=4)
-        if i >= min(args.warmup, 1):
-            vals.append(cb["value"])
-    value = sorted(vals)[len(vals) // 2]
-    cb["value"] = value
+    steps = max(1, min(args.steps, 5))
+    warm = min(1, max(0, args.warmup))
+    _cpu_prepare(S)
+    torch.set_num_threads(os.cpu_count() or 1)
+    runs = []
+    for i in range(warm + steps):
+        t = {}
+        _cpu_layer_once(S, t)
+        if i >= warm:
+            runs.append(t)
+    runs.sort(key=lambda t: t["select"] + t["attn"])
+    med = runs[len(runs) // 2]
+    per_layer = med["select"] + med["attn"]
+    value = args.frames / per_layer
+    import oracle
+
+    cb = {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "cpu": _cpu_model(),
+          "oracle_threads": oracle.num_threads(), "torch_threads": torch.get_num_threads(),
+          "select_s": round(med["select"], 4), "attn_s": round(med["attn"], 4),
+          "sample": (f"one whole cfg2 layer per step, median of {steps} steps after {warm} warm-up: oracle "
+                     f"scoring + HeSS + restore-swap and fp32 block-gathered torch attention over all "
+                     f"{S['L'].H * S['L'].nq} (head, q-block) rows")}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": steps, "warmup": min(args.warmup, 1), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "steps": steps, "warmup": warm, "ms_per_step": per_layer * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"cfg2 single global layer, {args.frames} views", "sparse_ratio": SPARSE_RATIO,
-                       "n_iters": 5, "note": "the reference's CPU path as restated by the oracle; steps capped at 2"},
+                       "n_iters": 5, "note": "the reference's path on the host cores: its selection as restated by "
+                                             "the oracle, its attention as fp32 block-gathered torch attention "
+                                             "(SpargeAttn has no CPU implementation); steps capped at 5"},
             "cpu_baseline": cb,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -334,7 +407,8 @@ def run_ress(args):
     attn_ms = _time_region(attn, reps, stream) / reps
     K.check_status(device)
     bf16_peak, hbm_peak, peak_src = _peaks()
-    mixed_peak = 2.0 / (1.0 / bf16_peak + 1.0 / (2.0 * bf16_peak))
+    int8_peak = _int8_peak(device)
+    mixed_peak = 2.0 / (1.0 / bf16_peak + 1.0 / int8_peak)
     achieved = attn_flops / (attn_ms / 1000.0) / 1e12
 
     # stage breakdown (eager calls, the second of two instrumented steps).  A
@@ -461,11 +535,13 @@ def run_ress(args):
             "gpu_launches": 12 * args.steps,
             "roofline": {"bound": "tensor", "kernel": "sparse_attn_kernel", "achieved": achieved,
                          "peak": mixed_peak, "unit": "TFLOP/s", "frac": achieved / mixed_peak,
-                         "traffic": ATTN_DRAM_BYTES_PER_LAUNCH * args.frames / N_FRAMES,
-                         "traffic_note": "dram read+write bytes per launch, ncu on the 24-frame layer scaled by tokens",
+                         "traffic": ATTN_DRAM_BYTES_PER_LAUNCH * args.frames / N_FRAMES / ws,
+                         "traffic_note": "dram read+write bytes per launch on this rank (its share of the heads), "
+                                         "ncu on the 24-frame layer scaled by tokens",
                          "attn_ms": attn_ms, "attn_tflop_per_launch": attn_flops / 1e12,
-                         "peak_note": f"{peak_src}: harmonic mix of bf16 burst {bf16_peak:.0f} TF/s (PV half) and "
-                                      "int8 = 2x bf16 (QK half)"},
+                         "peak_note": f"harmonic mix of the bf16 burst peak {bf16_peak:.0f} TF/s ({peak_src}, "
+                                      f"P.V half) and the int8 peak {int8_peak:.0f} TOP/s measured in this run "
+                                      "(torch._int_mm 8192^3, best of 10; Q.K^T half)"},
             "clocks": clk.summary(),
             "e2e": {"value": args.frames * e_steps / (e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e_steps,
@@ -557,7 +633,8 @@ def run_sweep(args):
     torch.cuda.set_device(device)
     stream = torch.cuda.current_stream(device)
     bf16_peak, _, peak_src = _peaks()
-    mixed = 2.0 / (1.0 / bf16_peak + 1.0 / (2.0 * bf16_peak))
+    int8_peak = _int8_peak(device)
+    mixed = 2.0 / (1.0 / bf16_peak + 1.0 / int8_peak)
     g = torch.Generator(device=device).manual_seed(0)
     for T in (8192, 32768, 131072, 300032):
         q, k, v = (torch.randn(1, 16, T, 64, device=device, generator=g, dtype=torch.float32).to(torch.bfloat16)
@@ -585,7 +662,8 @@ def run_sweep(args):
             print(json.dumps({"metric": "block-sparse attention op (config 5)", "Tp": T, "density": dens,
                               "kept_blocks": int(counts.sum().item()), "ms": round(ms, 4),
                               "tflops": round(tf, 1), "frac": round(tf / mixed, 4),
-                              "peak_note": f"{peak_src} mixed int8/bf16 peak {mixed:.0f} TF/s"}), flush=True)
+                              "peak_note": f"mixed peak {mixed:.0f} TF/s: bf16 {bf16_peak:.0f} ({peak_src}), int8 "
+                                           f"{int8_peak:.0f} (measured)"}), flush=True)
             del lists, counts, m, out
         del q8, qs, k8, ks, v16
         torch.cuda.empty_cache()

@@ -254,6 +254,44 @@ def sparse_attn_rows(q8, qs, k8, ks, v16, lists, counts, samples, sm_scale=None)
     return out
 
 
+def gathered_attention_fp32(q_patch, key, value, lists, counts, sm_scale=None, threads=None):
+    """Block-sparse attention in fp32 on the host cores, the CPU form of
+    run_block_sparse_kernel (attention.py:217-243): for every (head, 128-query
+    block) row, the listed 64-key blocks of K and V are gathered and
+    softmax(Q K^T * sm_scale) V is computed with torch's fp32 matmuls; keys
+    past Tk are masked.  q_patch (B, H, Tq, 64), key/value (B, H, Tk, 64) in
+    any float dtype; lists/counts as ress_b200 emits them, rows = B*H*nq.
+    Returns (B*H, Tq, 64) fp32.  A timing baseline, not a parity reference
+    (the GPU path quantises Q and K to int8 as SpargeAttn does)."""
+    if threads is not None:
+        torch.set_num_threads(threads)
+    B, H, Tq, D = q_patch.shape
+    BH = B * H
+    Tk = key.shape[-2]
+    nq = -(-Tq // KS_Q)
+    nkb = -(-Tk // KS_K)
+    pad = nkb * KS_K - Tk
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    qf = q_patch.reshape(BH, Tq, D).float()
+    kb = torch.nn.functional.pad(key.reshape(BH, Tk, D).float(), (0, 0, 0, pad)).view(BH, nkb, KS_K, D)
+    vb = torch.nn.functional.pad(value.reshape(BH, Tk, D).float(), (0, 0, 0, pad)).view(BH, nkb, KS_K, D)
+    lists = lists.view(BH, nq, -1)
+    counts = counts.view(BH, nq)
+    out = torch.zeros(BH, Tq, D, dtype=torch.float32)
+    for h in range(BH):
+        for b in range(nq):
+            c = int(counts[h, b])
+            if c <= 0:
+                continue
+            idx = lists[h, b, :c].long()
+            s = (qf[h, b * KS_Q:(b + 1) * KS_Q] @ kb[h, idx].reshape(-1, D).T) * sm_scale
+            if pad and int(idx[-1]) == nkb - 1:
+                s[:, -pad:] = float("-inf")
+            out[h, b * KS_Q:(b + 1) * KS_Q] = torch.softmax(s, -1) @ vb[h, idx].reshape(-1, D)
+    return out
+
+
 # --------------------------------------------------------------------------- layer
 
 def layer_select(q_patch, k_patch, v_patch, n_special_keys, M, head_scores=None, mode="ress",
