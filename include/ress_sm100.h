@@ -302,6 +302,29 @@ int ress_sparse_attn_split(const int8_t *q8, const float *qscale, const int8_t *
                            int32_t *status, int32_t *item_order, int split_chunk, float *partial,
                            int32_t *row_done, ress_stream_t stream);
 
+/*
+ * Dense (non-causal) attention in bf16 on the tensor cores: for each of BH
+ * sequences, softmax(q k^T * sm_scale) v over every key, bf16 Q.K^T and P.V
+ * with fp32 accumulation.  Replaces torch SDPA for the special-token queries
+ * of the global layer (src/ress/models/attention.py:404-412: each frame's
+ * special tokens attend densely to all keys) and for the aggregator's frame
+ * attention (the dense blocks that alternate with the global ones,
+ * src/ress/models/vggt.py:72-86).
+ *   q: row t of sequence bh at q + bh*q_sbh + t*q_st (bf16 elements, 64 per
+ *   row, contiguous); k, v likewise with kv_st / kv_sbh.  Bases 16-byte
+ *   aligned, strides multiples of 8 elements.
+ *   out: fp32, or bf16 when out_bf16; row t of sequence bh written at
+ *   out + (bh / out_heads)*out_sb + (bh % out_heads)*out_sh + t'*out_st,
+ *   t' = (t / out_group)*out_period + out_off + t % out_group
+ *   (a plain (BH, Tq, 64) output: out_heads = BH, out_group = Tq,
+ *   out_period = out_off = 0).
+ */
+int ress_dense_attn(const uint16_t *q, const uint16_t *k, const uint16_t *v, int BH, int Tq, int Tk,
+                    long long q_st, long long q_sbh, long long kv_st, long long kv_sbh, float sm_scale,
+                    void *out, int out_bf16, int out_heads, long long out_sb, long long out_sh,
+                    long long out_st, int out_group, long long out_period, int out_off, int32_t *status,
+                    ress_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,6 +60,8 @@ SIGNATURES = {
                                     _I, _P, _P, _P]),
     "ress_sparse_attn_split": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _I, _F, _P, _L, _L, _I,
                                     _I, _P, _P, _I, _P, _P, _P]),
+    "ress_dense_attn": (_I, [_P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _F, _P, _I, _I, _L, _L, _L, _I, _L, _I,
+                             _P, _P]),
 }
 
 _lib = None

@@ -67,20 +67,33 @@ constexpr int PV_WARP = 2;
 constexpr int REGS_CTRL = 32;
 constexpr int REGS_SOFT = 104;
 static_assert(128 * REGS_CTRL + 256 * REGS_SOFT <= NT * 80, "register split above the launch's registers");
-constexpr int NS = 4;                  // K/V ring stages
-constexpr int NP = 3;                  // P ring stages
-constexpr int Q_BYTES = 128 * 64;      // int8
-constexpr int K_BYTES = 64 * 64;       // int8
-constexpr int V_BYTES = 64 * 64 * 2;   // fp16
-constexpr int P_BYTES = 128 * 64 * 2;  // fp16
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + Q_BYTES;
-constexpr int OFF_V = OFF_K + NS * K_BYTES;
-constexpr int OFF_P = OFF_V + NS * V_BYTES;
-constexpr int ONES_BYTES = 16 * 64 * 2;  // fp16 ones: one K = 16 slice of the P.V's row-sum columns
-constexpr int OFF_ONES = OFF_P + NP * P_BYTES;
-constexpr int SMEM_TILES = OFF_ONES + ONES_BYTES;
-constexpr int SMEM_BYTES = SMEM_TILES + 1024;  // + alignment slack
+// Two modes share the kernel.
+//   SPARSE: int8 Q and K with per-block fp32 scales (S = int32 on the
+//           tensor core), fp16 V and P, keep lists.
+//   DENSE : bf16 Q, K, V and P (S = fp32 on the tensor core), every key
+//           block of the sequence, no scales.
+// Per mode: tile bytes and ring depths (two CTAs per SM must fit in shared
+// memory: the dense mode's bf16 Q/K tiles are twice as large, so its rings
+// are one stage shallower).
+enum Mode { SPARSE = 0, DENSE = 1 };
+constexpr int NS_MAX = 4, NP_MAX = 3;
+template <int MODE> struct Cfg {
+    static constexpr int NS = MODE == SPARSE ? 4 : 3;               // K/V ring stages
+    static constexpr int NP = MODE == SPARSE ? 3 : 2;               // P ring stages
+    static constexpr int Q_BYTES = 128 * 64 * (MODE == SPARSE ? 1 : 2);
+    static constexpr int K_BYTES = 64 * 64 * (MODE == SPARSE ? 1 : 2);
+    static constexpr int V_BYTES = 64 * 64 * 2;                     // fp16 / bf16
+    static constexpr int P_BYTES = 128 * 64 * 2;                    // fp16 / bf16
+    static constexpr int ONES_BYTES = 16 * 64 * 2;  // ones: one K = 16 slice of the P.V's row-sum columns
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int OFF_V = OFF_K + NS * K_BYTES;
+    static constexpr int OFF_P = OFF_V + NS * V_BYTES;
+    static constexpr int OFF_ONES = OFF_P + NP * P_BYTES;
+    static constexpr int SMEM_BYTES = OFF_ONES + ONES_BYTES + 1024;  // + alignment slack
+    static_assert(NS <= NS_MAX && NP <= NP_MAX, "ring deeper than the barrier arrays");
+    static_assert(2 * (SMEM_BYTES + 1024 + 256) <= 228 * 1024, "two CTAs per SM must fit in shared memory");
+};
 constexpr uint32_t TMEM_COLS = 256;            // S[2] (64 each) + O (80), power of two
 constexpr float RESCALE_THRESH = 8.0f;         // lazy rescale when the max grows by > 2^8
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;
@@ -273,12 +286,15 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint
 }
 constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
 
-// Instruction descriptors (M = 128, N = 64).
+// Instruction descriptors (M = 128).
 //   kind::i8 : D s32 (bits 4-5 = 2), A/B signed (bits 7, 10), both K-major.
-//   kind::f16: D f32 (1), A/B f16 (0), A K-major, B MN-major (bit 16).
+//   kind::f16: D f32 (1), A/B f16 (0) or bf16 (1 at bits 7 and 10), B MN-major (bit 16) for V.
 constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+//   S = Q K^T in bf16, N = 64, both K-major.
+constexpr uint32_t IDESC_QK_BF16 = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
 //   P.V uses N = 80: the 16 extra B columns are ones, so O columns 64..79 hold sum(P).
 constexpr uint32_t IDESC_F16 = (1u << 4) | (1u << 16) | ((80u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t IDESC_PV_BF16 = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((80u >> 3) << 17) | ((128u >> 4) << 24);
 
 // ------------------------------------------------------------- softmax pieces
 // Constants of the S read-out: S arrives as int32 in TMEM; adding MAGIC_I
@@ -286,6 +302,21 @@ constexpr uint32_t IDESC_F16 = (1u << 4) | (1u << 16) | ((80u >> 3) << 17) | ((1
 // 64 * 127^2), so the scale-and-subtract of the softmax is one FMA.
 constexpr float MAGIC_F = 12582912.0f;
 constexpr uint32_t MAGIC_I = 0x4B400000u;
+// The dense mode's S is fp32 already: no offset to add or subtract.
+template <int MODE> struct SBits {
+    static constexpr uint32_t ADD = MODE == SPARSE ? MAGIC_I : 0u;
+    static constexpr float SUB = MODE == SPARSE ? MAGIC_F : 0.0f;
+};
+// P as the P.V MMA reads it: fp16 (sparse, with fp16 V) or bf16 (dense, with bf16 V).
+template <int MODE> __device__ __forceinline__ uint32_t pack_p(float a, float b) {
+    if constexpr (MODE == SPARSE) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t *>(&h);
+    } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+}
 
 // Per-thread softmax state handed to the out-of-line paths.
 struct RowCtx {
@@ -317,6 +348,7 @@ __device__ __noinline__ void rescale_o(uint32_t tO, uint32_t lane_addr, float al
 // Writes P = 2^(c*s + bias) for this thread's 32 key columns (col0 + t, 0
 // where col0 + t >= nvalid) of its row into the P tile at pbase (fp16,
 // 128B-swizzled K-major; 16-byte chunks ch0..ch0+3 of the row).
+template <int MODE>
 __device__ __forceinline__ void store_p_masked(const uint32_t (&sv)[32], int nvalid, int col0, float c, float bias,
                                                uint32_t pbase, uint32_t rsw, uint32_t ch0) {
 #pragma unroll
@@ -329,8 +361,7 @@ __device__ __forceinline__ void store_p_masked(const uint32_t (&sv)[32], int nva
             fma2(x0, x1, __uint_as_float(sv[i0]), __uint_as_float(sv[i0 + 1]), c, bias);
             x0 = col0 + i0 < nvalid ? x0 : -INFINITY;
             x1 = col0 + i0 + 1 < nvalid ? x1 : -INFINITY;
-            __half2 hp = __floats2half2_rn(ex2(x0), ex2(x1));
-            h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
+            h[t >> 1] = pack_p<MODE>(ex2(x0), ex2(x1));
         }
         const uint32_t a = pbase + (((ch0 + (uint32_t)ch) ^ rsw) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
@@ -343,8 +374,10 @@ __device__ __forceinline__ void store_p_masked(const uint32_t (&sv)[32], int nva
 // TMEM buffer sb itself (the caller has waited for it) and releases it.
 // Out of line so that the hot loop holds only the full-block path.
 // Returns false when a bounded wait failed.
+template <int MODE>
 __device__ __noinline__ float softmax_block_general(const RowCtx &rc, int j, int sb, int pb, int nvalid, float c,
                                                     float m, uint64_t *s_free) {
+    constexpr int NP = Cfg<MODE>::NP;
     uint32_t sv[32];
     tmem_ld_half32(rc.tS + sb * 64 + rc.lane_addr, sv);
     tmem_wait_ld();
@@ -353,11 +386,11 @@ __device__ __noinline__ float softmax_block_general(const RowCtx &rc, int j, int
     float fmx = -INFINITY;
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
-        sv[t] += MAGIC_I;
+        sv[t] += SBits<MODE>::ADD;
         if (rc.col0 + t < nvalid) fmx = fmaxf(fmx, __uint_as_float(sv[t]));
     }
     fmx = fmaxf(fmx, __shfl_xor_sync(0xffffffffu, fmx, 16));  // the row's other half
-    const float mx = c * (fmx - MAGIC_F);
+    const float mx = c * (fmx - SBits<MODE>::SUB);
     const bool grow = mx > m + RESCALE_THRESH;
     const float m_new = grow ? mx : m;
     if (__any_sync(0xffffffffu, grow && j > 0)) {
@@ -366,15 +399,16 @@ __device__ __noinline__ float softmax_block_general(const RowCtx &rc, int j, int
         fence_after();
         rescale_o(rc.tO, rc.lane_addr, grow ? ex2(m - m_new) : 1.0f);
     }
-    store_p_masked(sv, nvalid, rc.col0, c, fmaf(-c, MAGIC_F, -m_new), rc.sP + pb * P_BYTES + rc.prow, rc.rsw, rc.ch0);
+    store_p_masked<MODE>(sv, nvalid, rc.col0, c, fmaf(-c, SBits<MODE>::SUB, -m_new),
+                         rc.sP + pb * Cfg<MODE>::P_BYTES + rc.prow, rc.rsw, rc.ch0);
     fence_before();
     return m_new;
 }
 
 struct Bars {
     uint64_t q_full;
-    uint64_t kv_full[NS], kv_empty[NS];
-    uint64_t s_full[2], s_free[2], p_full[NP], o_full[NP];
+    uint64_t kv_full[NS_MAX], kv_empty[NS_MAX];
+    uint64_t s_full[2], s_free[2], p_full[NP_MAX], o_full[NP_MAX];
     uint64_t s_done, pv_done;
     uint32_t tmem_base;
     int abort_flag;
@@ -402,26 +436,34 @@ __host__ __device__ __forceinline__ int split_pieces(int full, int chunk) {
     return (full + sz - 1) / sz;
 }
 
+// Output addressing shared by both modes: query row t of sequence bh lands at
+//   out + (bh / out_heads) * out_sb + (bh % out_heads) * out_sh + t' * out_st,
+//   t' = (t / out_hw) * out_period + out_off + t % out_hw,
+// in fp32, or in bf16 when out_bf16 (dense mode).
+template <int MODE>
 __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const float *__restrict__ qscale,
     const float *__restrict__ kscale, int nqb, int nkb, int Tq, int Tk, const int32_t *__restrict__ lists,
-    const int32_t *__restrict__ counts, int list_width, float sm_scale_log2, float *__restrict__ out,
-    long long out_sh, long long out_st, int out_hw, int out_special, int32_t *__restrict__ status,
-    const int32_t *__restrict__ row_order, int split_chunk, float *__restrict__ partial,
-    int32_t *__restrict__ row_done) {
+    const int32_t *__restrict__ counts, int list_width, float sm_scale_log2, void *__restrict__ out_raw,
+    long long out_sb, long long out_sh, long long out_st, int out_heads, int out_hw, long long out_period,
+    int out_off, int out_bf16, int32_t *__restrict__ status, const int32_t *__restrict__ row_order,
+    int split_chunk, float *__restrict__ partial, int32_t *__restrict__ row_done) {
+    using C = Cfg<MODE>;
+    constexpr int NS = C::NS, NP = C::NP;
     extern __shared__ unsigned char dyn_raw[];
     __shared__ Bars B;
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)dyn_raw + 1023) & ~(uintptr_t)1023);
-    const uint32_t sQ = smem_u32(smem + OFF_Q);
-    const uint32_t sK = smem_u32(smem + OFF_K);
-    const uint32_t sV = smem_u32(smem + OFF_V);
-    const uint32_t sP = smem_u32(smem + OFF_P);
-    const uint32_t sOnes = smem_u32(smem + OFF_ONES);
+    const uint32_t sQ = smem_u32(smem + C::OFF_Q);
+    const uint32_t sK = smem_u32(smem + C::OFF_K);
+    const uint32_t sV = smem_u32(smem + C::OFF_V);
+    const uint32_t sP = smem_u32(smem + C::OFF_P);
+    const uint32_t sOnes = smem_u32(smem + C::OFF_ONES);
     {
-        // ones tile (fp16 1.0), read by the tensor core through the async proxy
-        uint4 *o4 = reinterpret_cast<uint4 *>(smem + OFF_ONES);
-        for (int i = threadIdx.x; i < ONES_BYTES / 16; i += NT) o4[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+        // ones tile (1.0 in the P.V operand type), read by the tensor core through the async proxy
+        const uint32_t one2 = MODE == SPARSE ? 0x3C003C00u : 0x3F803F80u;
+        uint4 *o4 = reinterpret_cast<uint4 *>(smem + C::OFF_ONES);
+        for (int i = threadIdx.x; i < C::ONES_BYTES / 16; i += NT) o4[i] = make_uint4(one2, one2, one2, one2);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -440,13 +482,13 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     } else {
         row = row_order != nullptr ? row_order[blockIdx.x] : (int)blockIdx.x;
     }
-    const int full_cnt = min(counts[row], list_width);
+    const int full_cnt = MODE == DENSE ? nkb : min(counts[row], list_width);
     const int pieces = split_launch ? split_pieces(max(full_cnt, 0), split_chunk) : 1;
     if (piece >= pieces) return;  // an empty item: the whole CTA leaves before any barrier
     const bool split = pieces > 1;
     const int psz = split ? split_size(full_cnt, split_chunk) : full_cnt;
     const int cnt = split ? min(psz, full_cnt - piece * psz) : full_cnt;
-    const int32_t *lst = lists + (size_t)row * list_width + (size_t)piece * (split ? psz : 0);
+    const int32_t *lst = MODE == DENSE ? nullptr : lists + (size_t)row * list_width + (size_t)piece * (split ? psz : 0);
     const int bh = row / nqb, qb = row - bh * nqb;
     volatile int *abort_flag = &B.abort_flag;
 
@@ -490,16 +532,16 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0 && cnt > 0) {
-            mbar_expect_tx(&B.q_full, Q_BYTES);
+            mbar_expect_tx(&B.q_full, C::Q_BYTES);
             tma_load_3d(sQ, &tm_q, &B.q_full, 0, qb * 128, bh);
             int j = 0;
             for (; j < cnt; ++j) {
                 const int st = j % NS;
                 if (j >= NS && !wait_bar(&B.kv_empty[st], ((j - NS) / NS) & 1, abort_flag, status)) break;
-                const int kb = lst[j];
-                mbar_expect_tx(&B.kv_full[st], K_BYTES + V_BYTES);
-                tma_load_3d(sK + st * K_BYTES, &tm_k, &B.kv_full[st], 0, kb * 64, bh);
-                tma_load_3d(sV + st * V_BYTES, &tm_v, &B.kv_full[st], 0, kb * 64, bh);
+                const int kb = MODE == DENSE ? j : lst[j];
+                mbar_expect_tx(&B.kv_full[st], C::K_BYTES + C::V_BYTES);
+                tma_load_3d(sK + st * C::K_BYTES, &tm_k, &B.kv_full[st], 0, kb * 64, bh);
+                tma_load_3d(sV + st * C::V_BYTES, &tm_v, &B.kv_full[st], 0, kb * 64, bh);
             }
             // drain: the last load issued on each stage must have landed
             // before the CTA may exit (already true on the normal path)
@@ -530,11 +572,20 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                 // softmax of block j) waits until that P.V has completed
                 if (j >= NP && !wait_bar(&B.o_full[j % NP], ((j - NP) / NP) & 1, abort_flag, status)) break;
                 fence_after();
+                if constexpr (MODE == SPARSE) {
 #pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {
-                    const uint64_t ad = make_desc(sQ + kk * 32, 16, 512, LAYOUT_SW64);
-                    const uint64_t bd = make_desc(sK + st * K_BYTES + kk * 32, 16, 512, LAYOUT_SW64);
-                    mma_i8(tS + sb * 64, ad, bd, IDESC_I8, kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < 2; ++kk) {  // int8, K = 32 per MMA, 64B-swizzled rows
+                        const uint64_t ad = make_desc(sQ + kk * 32, 16, 512, LAYOUT_SW64);
+                        const uint64_t bd = make_desc(sK + st * C::K_BYTES + kk * 32, 16, 512, LAYOUT_SW64);
+                        mma_i8(tS + sb * 64, ad, bd, IDESC_I8, kk > 0 ? 1u : 0u);
+                    }
+                } else {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {  // bf16, K = 16 per MMA, 128B-swizzled rows
+                        const uint64_t ad = make_desc(sQ + kk * 32, 16, 1024, LAYOUT_SW128);
+                        const uint64_t bd = make_desc(sK + st * C::K_BYTES + kk * 32, 16, 1024, LAYOUT_SW128);
+                        mma_f16(tS + sb * 64, ad, bd, IDESC_QK_BF16, kk > 0 ? 1u : 0u);
+                    }
                 }
                 mma_commit(&B.s_full[sb]);
             }
@@ -555,8 +606,8 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                 // this thread itself orders the tensor core's read after the copy)
                 if (!wait_bar(&B.kv_full[st], (j / NS) & 1, abort_flag, status)) break;
                 fence_after();
-                const uint32_t pa = sP + pb * P_BYTES;
-                const uint32_t va = sV + st * V_BYTES;
+                const uint32_t pa = sP + pb * C::P_BYTES;
+                const uint32_t va = sV + st * C::V_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t ad = make_desc(pa + kk * 32, 16, 1024, LAYOUT_SW128);
@@ -564,7 +615,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                     // past the first; every K slice reads the same 16-row ones tile
                     const uint32_t vk = va + kk * 2048;
                     const uint64_t bd = make_desc(vk, sOnes - vk, 1024, LAYOUT_SW128);
-                    mma_f16(tO, ad, bd, IDESC_F16, (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_f16(tO, ad, bd, MODE == SPARSE ? IDESC_F16 : IDESC_PV_BF16, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(&B.o_full[pb]);
                 mma_commit(&B.kv_empty[st]);
@@ -591,26 +642,29 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         const int r = lane0 + (lane & 15);
         const int col0 = (lane >> 4) * 32;
         const uint32_t lane_addr = (uint32_t)lane0 << 16;
-        const float qs = qscale[(size_t)bh * nqb + qb];
+        const float qs = MODE == SPARSE ? qscale[(size_t)bh * nqb + qb] : 1.0f;
         float m = -INFINITY;
         bool ok = true;
         const uint32_t prow = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
         const uint32_t rsw = (uint32_t)(r & 7);
         const uint32_t ch0 = (uint32_t)(col0 >> 3);  // first 16-byte chunk of the half row
         const RowCtx rc{tS, tO, lane_addr, sP, prow, rsw, ch0, col0, B.o_full, abort_flag, status};
-        const float *ksc = kscale + (size_t)bh * nkb;
+        const float *ksc = MODE == SPARSE ? kscale + (size_t)bh * nkb : nullptr;
+        // per-block scale of S (the K block's quantisation scale; 1 in the dense mode)
+        auto kscale_of = [&](int kb) { return MODE == SPARSE ? ksc[kb] : 1.0f; };
+        auto list_at = [&](int i) { return MODE == SPARSE ? lst[i] : i; };
 
         // block 0 and a ragged last block (keys past Tk) take the general path;
         // blocks [1, hot_end) are full blocks after the first
-        const int kb_last = cnt > 0 ? lst[cnt - 1] : 0;
+        const int kb_last = cnt > 0 ? list_at(cnt - 1) : 0;
         const int hot_end = (cnt > 1 && Tk - kb_last * 64 < 64) ? cnt - 1 : cnt;
         if (cnt > 0) {
-            const int kb0 = lst[0];
-            const float c0 = qs * ksc[kb0] * sm_scale_log2;
+            const int kb0 = list_at(0);
+            const float c0 = qs * kscale_of(kb0) * sm_scale_log2;
             if (!wait_bar_warp(&B.s_full[0], 0, abort_flag, status)) ok = false;
             fence_after();
             if (ok) {
-                m = softmax_block_general(rc, 0, 0, 0, min(64, Tk - kb0 * 64), c0, m, &B.s_free[0]);
+                m = softmax_block_general<MODE>(rc, 0, 0, 0, min(64, Tk - kb0 * 64), c0, m, &B.s_free[0]);
                 ok = m == m;  // NaN: a bounded wait failed
             }
             if (ok) {
@@ -620,8 +674,8 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         }
         // two-deep prefetch: block j+2's index and block j+1's scale are
         // loaded one iteration before they are needed
-        int kb_nxt = cnt > 2 ? lst[2] : 0;
-        float ks_cur = cnt > 1 ? ksc[lst[1]] : 0.0f;
+        int kb_nxt = cnt > 2 ? list_at(2) : 0;
+        float ks_cur = cnt > 1 ? kscale_of(list_at(1)) : 0.0f;
         bool s_ready = false;  // S_j's phase already seen complete by an early probe
         int pb = 1 % NP;
         // swizzled offsets of this thread's four 16-byte chunks in its P row
@@ -632,8 +686,10 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
         for (; ok && j < hot_end; ++j) {
             const int sb = j & 1;
             const float c = qs * ks_cur * sm_scale_log2;
-            ks_cur = (j + 1 < cnt) ? ksc[kb_nxt] : 0.0f;
-            kb_nxt = (j + 2 < cnt) ? lst[j + 2] : 0;
+            if constexpr (MODE == SPARSE) {
+                ks_cur = (j + 1 < cnt) ? ksc[kb_nxt] : 0.0f;
+                kb_nxt = (j + 2 < cnt) ? lst[j + 2] : 0;
+            }
             if (!__all_sync(0xffffffffu, s_ready) && !wait_bar_warp(&B.s_full[sb], (j >> 1) & 1, abort_flag, status)) {
                 ok = false;
                 break;
@@ -645,7 +701,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             fence_before();
             mbar_arrive(&B.s_free[sb]);
 #pragma unroll
-            for (int u = 0; u < 32; ++u) sv[u] += MAGIC_I;
+            for (int u = 0; u < 32; ++u) sv[u] += SBits<MODE>::ADD;
             float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
             for (int t = 0; t < 32; t += 8) {
@@ -656,7 +712,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             }
             float fmx = max3(a0, a1, fmaxf(a2, a3));
             fmx = fmaxf(fmx, __shfl_xor_sync(0xffffffffu, fmx, 16));  // the row's other half
-            const float mx = c * (fmx - MAGIC_F);
+            const float mx = c * (fmx - SBits<MODE>::SUB);
             // lazy rescale: the maximum moves only when it grew by more than the threshold
             const bool grow = mx > m + RESCALE_THRESH;
             if (__any_sync(0xffffffffu, grow)) {
@@ -668,7 +724,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                 m = m_new;
             }
             // P_{j-NP} (same tile) was consumed: S_j is issued only after its P.V completed
-            const float bias = fmaf(-c, MAGIC_F, -m);
+            const float bias = fmaf(-c, SBits<MODE>::SUB, -m);
             // probe S_{j+1} now; the answer is used after this block's exponentials
             s_ready = mbar_test_wait(smem_u32(&B.s_full[sb ^ 1]), ((j + 1) >> 1) & 1);
 #pragma unroll
@@ -679,10 +735,9 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
                     const int i0 = ch * 8 + t;
                     float x0, x1;
                     fma2(x0, x1, __uint_as_float(sv[i0]), __uint_as_float(sv[i0 + 1]), c, bias);
-                    __half2 hp = __floats2half2_rn(ex2(x0), ex2(x1));
-                    h[t >> 1] = *reinterpret_cast<uint32_t *>(&hp);
+                    h[t >> 1] = pack_p<MODE>(ex2(x0), ex2(x1));
                 }
-                const uint32_t a = sP + pb * P_BYTES + poff[ch];
+                const uint32_t a = sP + pb * C::P_BYTES + poff[ch];
                 asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]),
                              "r"(h[3])
                              : "memory");
@@ -699,7 +754,7 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
             if (!wait_bar_warp(&B.s_full[sb], (j >> 1) & 1, abort_flag, status)) ok = false;
             fence_after();
             if (ok) {
-                m = softmax_block_general(rc, j, sb, j % NP, Tk - kb_last * 64, c, m, &B.s_free[sb]);
+                m = softmax_block_general<MODE>(rc, j, sb, j % NP, Tk - kb_last * 64, c, m, &B.s_free[sb]);
                 ok = m == m;
             }
             if (ok) {
@@ -731,17 +786,34 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        const long long tt = (long long)(t / out_hw) * (out_hw + out_special) + out_special + (t % out_hw);
-        float *dst = out + (size_t)bh_e * out_sh + tt * out_st + col0;
+        const long long tt = (long long)(t / out_hw) * out_period + out_off + (t % out_hw);
+        const long long dst_off = (long long)(bh_e / out_heads) * out_sb + (long long)(bh_e % out_heads) * out_sh +
+                                  tt * out_st + col0;
+        float *dst = reinterpret_cast<float *>(out_raw) + dst_off;
         const int pieces_e = split_launch ? split_pieces(max(min(__ldg(&counts[row_e]), list_width), 0), split_chunk) : 1;
         if (pieces_e == 1) {
             const float inv = (ok && cnt > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
             if (t < Tq) {
+                if (MODE == DENSE && out_bf16) {
+                    __nv_bfloat16 *db = reinterpret_cast<__nv_bfloat16 *>(out_raw) + dst_off;
 #pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4 *>(dst + i) =
-                        make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                                    __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+                    for (int i = 0; i < 32; i += 8) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o[i + 2 * u]) * inv,
+                                                                      __uint_as_float(o[i + 2 * u + 1]) * inv);
+                            w[u] = *reinterpret_cast<uint32_t *>(&b2);
+                        }
+                        *reinterpret_cast<uint4 *>(db + i) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4 *>(dst + i) =
+                            make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                                        __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+                }
             }
         } else {
             // this piece's partial (O unnormalised, m, l) for query r
@@ -884,12 +956,15 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
+// 3-D map {64, T, BH} over rows of 64 elements; row and sequence strides in
+// elements (contiguous (BH, T, 64) when row_stride = 64, seq_stride = T * 64).
 static bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, int T, int BH,
-                     int box_rows, CUtensorMapSwizzle sw) {
+                     int box_rows, CUtensorMapSwizzle sw, long long row_stride = 64, long long seq_stride = -1) {
     auto enc = get_encode();
     if (!enc) return false;
+    if (seq_stride < 0) seq_stride = (long long)T * 64;
     cuuint64_t dims[3] = {64, (cuuint64_t)T, (cuuint64_t)BH};
-    cuuint64_t strides[2] = {(cuuint64_t)64 * elem_bytes, (cuuint64_t)T * 64 * elem_bytes};
+    cuuint64_t strides[2] = {(cuuint64_t)row_stride * elem_bytes, (cuuint64_t)seq_stride * elem_bytes};
     cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
@@ -931,12 +1006,14 @@ static int sparse_attn_impl(const int8_t *q8, const float *qscale, const int8_t 
     } else {
         row_order = nullptr;
     }
-    set_smem_attr((const void *)attn::sparse_attn_kernel, attn::SMEM_BYTES);
+    constexpr int SMEM = attn::Cfg<attn::SPARSE>::SMEM_BYTES;
+    set_smem_attr((const void *)attn::sparse_attn_kernel<attn::SPARSE>, SMEM);
     const float log2e = 1.4426950408889634f;
-    attn::sparse_attn_kernel<<<split ? attn::SPLIT_MAX * rows : rows, attn::NT, attn::SMEM_BYTES,
-                               (cudaStream_t)stream>>>(
-        tq, tk, tv, qscale, kscale, nqb, nkb, Tq, Tk, lists, counts, list_width, sm_scale * log2e, out, out_sh,
-        out_st, out_hw, out_special, status, row_order, split_chunk, partial, row_done);
+    attn::sparse_attn_kernel<attn::SPARSE><<<split ? attn::SPLIT_MAX * rows : rows, attn::NT, SMEM,
+                                             (cudaStream_t)stream>>>(
+        tq, tk, tv, qscale, kscale, nqb, nkb, Tq, Tk, lists, counts, list_width, sm_scale * log2e, out, 0, out_sh,
+        out_st, BH, out_hw, (long long)out_hw + out_special, out_special, 0, status, row_order, split_chunk, partial,
+        row_done);
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }
 
@@ -971,4 +1048,37 @@ extern "C" int ress_sparse_attn_split(const int8_t *q8, const float *qscale, con
     return sparse_attn_impl(q8, qscale, k8, kscale, v16, BH, Tq, Tk, lists, counts, list_width, sm_scale, out,
                             out_sh, out_st, out_hw, out_special, status, item_order, split_chunk, partial,
                             row_done, stream);
+}
+
+extern "C" int ress_dense_attn(const uint16_t *q, const uint16_t *k, const uint16_t *v, int BH, int Tq, int Tk,
+                               long long q_st, long long q_sbh, long long kv_st, long long kv_sbh, float sm_scale,
+                               void *out, int out_bf16, int out_heads, long long out_sb, long long out_sh,
+                               long long out_st, int out_group, long long out_period, int out_off, int32_t *status,
+                               ress_stream_t stream) {
+    if (!q || !k || !v || !out || !status) return RESS_E_ARG;
+    if (BH <= 0 || Tq <= 0 || Tk <= 0 || out_heads <= 0 || out_group <= 0 || out_period < 0 || out_off < 0)
+        return RESS_E_ARG;
+    // TMA: 16-byte aligned bases and strides; vector stores of the output rows
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15) return RESS_E_ARG;
+    if (((q_st | q_sbh | kv_st | kv_sbh) * 2) & 15) return RESS_E_ARG;
+    if (q_st < 64 || kv_st < 64 || q_sbh < 0 || kv_sbh < 0) return RESS_E_ARG;
+    const int eb = out_bf16 ? 2 : 4;
+    if (((uintptr_t)out & 15) || ((out_sb | out_sh | out_st) * eb) & 15) return RESS_E_ARG;
+    if ((long long)Tk * kv_st > (1ll << 40) || Tq > (1 << 30)) return RESS_E_SHAPE;
+    CUtensorMap tq, tk, tv;
+    if (!attn::make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Tq, BH, 128, CU_TENSOR_MAP_SWIZZLE_128B, q_st,
+                        q_sbh) ||
+        !attn::make_map(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Tk, BH, 64, CU_TENSOR_MAP_SWIZZLE_128B, kv_st,
+                        kv_sbh) ||
+        !attn::make_map(&tv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Tk, BH, 64, CU_TENSOR_MAP_SWIZZLE_128B, kv_st,
+                        kv_sbh))
+        return RESS_E_NO_DEVICE;
+    const int nqb = (Tq + 127) / 128, nkb = (Tk + 63) / 64;
+    constexpr int SMEM = attn::Cfg<attn::DENSE>::SMEM_BYTES;
+    set_smem_attr((const void *)attn::sparse_attn_kernel<attn::DENSE>, SMEM);
+    const float log2e = 1.4426950408889634f;
+    attn::sparse_attn_kernel<attn::DENSE><<<BH * nqb, attn::NT, SMEM, (cudaStream_t)stream>>>(
+        tq, tk, tv, nullptr, nullptr, nqb, nkb, Tq, Tk, nullptr, nullptr, nkb, sm_scale * log2e, out, out_sb, out_sh,
+        out_st, out_heads, out_group, out_period, out_off, out_bf16, status, nullptr, 0, nullptr, nullptr);
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }

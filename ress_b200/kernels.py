@@ -445,6 +445,42 @@ def sparse_attn(q8, qscale, k8, kscale, v16, lists, counts, out=None, out_layout
     return out
 
 
+def dense_attn(q, k, v, out=None, out_bf16=None, sm_scale=None, out_rows=None):
+    """Dense non-causal attention, bf16 on the tensor cores (ress_dense_attn).
+    q (S, Tq, 64), k/v (S, Tk, 64) bf16 with a contiguous last dim and one
+    stride per sequence and per row (e.g. (B*H) sequences of a contiguous
+    (B, H, T, 64) tensor, viewed as (B*H, T, 64)).
+    out: None -> a new (S, Tq, 64) tensor (bf16 unless out_bf16 is False);
+    otherwise written in place, addressed by out_rows = (out_heads, out_sb,
+    out_sh, out_st, group, period, offset) (see include/ress_sm100.h)."""
+    _dev_ok(q, k, v)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise RessError("dense_attn takes bf16 q, k, v")
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3 or q.shape[-1] != HD or k.stride() != v.stride():
+        raise RessError("dense_attn takes (S, T, 64) q, k, v with k and v sharing strides")
+    if q.stride(-1) != 1 or k.stride(-1) != 1:
+        raise RessError("dense_attn needs a contiguous last dim")
+    S, Tq, _ = q.shape
+    Tk = k.shape[1]
+    dev = q.device
+    if out is None:
+        bf = True if out_bf16 is None else bool(out_bf16)
+        out = torch.empty(S, Tq, HD, dtype=torch.bfloat16 if bf else torch.float32, device=dev)
+        rows = (S, 0, out.stride(0), out.stride(1), Tq, 0, 0)
+    else:
+        bf = out.dtype == torch.bfloat16
+        if not bf and out.dtype != torch.float32:
+            raise RessError("dense_attn output must be fp32 or bf16")
+        rows = out_rows if out_rows is not None else (S, 0, out.stride(0), out.stride(1), Tq, 0, 0)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(HD)
+    heads, sb, sh, st, grp, period, off = rows
+    check(_lib.load().ress_dense_attn(_ptr(q), _ptr(k), _ptr(v), S, Tq, Tk, q.stride(1), q.stride(0), k.stride(1),
+                                      k.stride(0), ctypes.c_float(sm_scale), _ptr(out), int(bf), heads, sb, sh, st, grp,
+                                      period, off, _ptr(status_word(dev)), _stream(dev)), "ress_dense_attn")
+    return out
+
+
 def qkv_prologue(qkv, H, qn_weight=None, qn_bias=None, kn_weight=None, kn_bias=None, eps=1e-5, pos=None,
                  rope_cos=None, rope_sin=None):
     """(B, T, 3*H*64) qkv Linear output -> q, k, v (B, H, T, 64): q/k LayerNorm

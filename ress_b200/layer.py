@@ -135,14 +135,26 @@ def _random_gen(device):
     return g
 
 
-def special_attention(q, k, v, L: K.Layout):
-    """Dense SDPA of the special-token queries over all keys (attention.py:
-    404-409; the key order does not change a softmax)."""
+def special_attention(q, k, v, L: K.Layout, out=None):
+    """Dense attention of the special-token queries over all keys
+    (attention.py:404-409; the key order does not change a softmax).
+    bf16 layers with an fp32 full-layout ``out``: the library's dense bf16
+    kernel writes the rows straight into their places in ``out`` and None is
+    returned.  Otherwise (fp32 layers) torch SDPA's result is returned for
+    the caller to place."""
     if L.special == 0:
         return None
     B, H = L.B, L.H
-    qs = q.view(B, H, L.frames, L.special + L.hw, 64)[:, :, :, : L.special].reshape(B, H, L.Ts, 64)
-    return F.scaled_dot_product_attention(qs, k, v)
+    qs = q.view(B, H, L.frames, L.special + L.hw, 64)[:, :, :, : L.special]
+    if q.dtype == torch.bfloat16 and out is not None and out.dtype == torch.float32 and out.stride(-1) == 1:
+        q2 = qs.reshape(B * H, L.Ts, 64)  # gathers the special rows (small)
+        k2, v2 = k.flatten(0, 1), v.flatten(0, 1)
+        if k2.stride() != v2.stride():
+            k2, v2 = k2.contiguous(), v2.contiguous()
+        rows = (H, out.stride(0), out.stride(1), out.stride(2), L.special, L.special + L.hw, 0)
+        K.dense_attn(q2, k2, v2, out=out, out_rows=rows)
+        return None
+    return F.scaled_dot_product_attention(qs.reshape(B, H, L.Ts, 64), k, v)
 
 
 def select_blocks(attn_full, attn_cond, vbar, B: int, H: int, nq: int, n_cand: int, sink_blocks: int,
@@ -208,14 +220,17 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
     B, H = L.B, L.H
     n_cand = L.n_cand
     ws = K.workspace(dev, B * H, L.Tp, L.Tk, n_cand)
+    if out is None:
+        out = torch.empty(B, H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=dev)
     main = torch.cuda.current_stream(dev)
     capturing = torch.cuda.is_current_stream_capturing()
     side = _side_stream(dev)
     side.wait_stream(main)
     with torch.cuda.stream(side):
-        x_special = special_attention(q, k, v, L)
+        # special rows of `out` (disjoint from the patch rows the main stream writes)
+        x_special = special_attention(q, k, v, L, out)
     if not capturing:
-        for t in (q, k, v):
+        for t in (q, k, v, out):
             t.record_stream(side)
 
     qbar, q8, qs = K.pool_quant_q(q, L)
@@ -230,8 +245,6 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
         if map_hook is not None:
             fm = map_hook(fm.view(B, H, L.nq, width), attn_cond.view(B, H, L.nq, n_cand))
         lists, counts = K.map_to_lists(fm.reshape(-1, width))
-        if out is None:
-            out = torch.empty(B, H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=dev)
         K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out, out_layout=L, split=attn_split)
         main.wait_stream(side)
         if x_special is not None:
@@ -250,8 +263,6 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
         fm = map_hook(fm, attn_cond.view(B, H, L.nq, n_cand))
         lists, counts = K.map_to_lists(fm.reshape(-1, width))
         r = dict(lists=lists, counts=counts)
-    if out is None:
-        out = torch.empty(B, H, L.frames * (L.special + L.hw), 64, dtype=torch.float32, device=dev)
     K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"], out=out, out_layout=L, split=attn_split)
     main.wait_stream(side)
     if x_special is not None:

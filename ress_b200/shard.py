@@ -252,12 +252,15 @@ def view_sharded_layer(q, k, v, geom: ViewGeom, budget, order, gather, *, lead_b
     Lq = K.Layout(B, H, 1, 0, qp.shape[2])
     Ll = K.Layout(B, H, geom.frames_local, geom.special, geom.hw)
     ws = K.workspace(dev, B * H, Lk.Tp, Lk.Tk, Lk.n_cand)
+    F_, S_, HW = geom.frames_local, geom.special, geom.hw
+    out = torch.empty(B, H, F_ * (S_ + HW), 64, dtype=torch.float32, device=dev)
     main = torch.cuda.current_stream(dev)
     side = LY._side_stream(dev)
     side.wait_stream(main)
     with torch.cuda.stream(side):
-        x_special = LY.special_attention(q, k_full, v_full, Ll)
-    for t in (q, k_full, v_full):
+        # this rank's special rows of `out` (bf16 layers: written in place)
+        x_special = LY.special_attention(q, k_full, v_full, Ll, out)
+    for t in (q, k_full, v_full, out):
         t.record_stream(side)
     qbar, q8, qs = K.pool_quant_q(qp, Lq)
     kbar, vbar, k8, ks, v16, _ = K.pool_quant_kv(k_full, v_full, Lk, ws=ws)
@@ -265,8 +268,6 @@ def view_sharded_layer(q, k, v, geom: ViewGeom, budget, order, gather, *, lead_b
     nts, r = LY.select_blocks(attn_full, attn_cond, vbar, B, H, Lq.nq, Lk.n_cand, Lk.sink_blocks, budget, order,
                               lead_blocks=lead_blocks, ws=ws)
     o = K.sparse_attn(q8, qs, k8, ks, v16, r["lists"], r["counts"]).view(B, H, qp.shape[2], 64)
-    F_, S_, HW = geom.frames_local, geom.special, geom.hw
-    out = torch.empty(B, H, F_ * (S_ + HW), 64, dtype=torch.float32, device=dev)
     view = out.view(B, H, F_, S_ + HW, 64)
     view[:, :, :, S_:] = o[:, :, geom.lo: geom.lo + F_ * HW].view(B, H, F_, HW, 64)
     main.wait_stream(side)

@@ -82,7 +82,28 @@ class Attention(nn.Module):
     def forward(self, x, pos=None):
         B, T, C = x.shape
         nh = self.num_heads
-        q, k, v = self.qkv(x).view(B, T, 3, nh, C // nh).permute(2, 0, 3, 1, 4).unbind(0)
+        hd = C // nh
+        lin = self.qkv(x)
+        if x.is_cuda and x.dtype == torch.bfloat16 and hd == 64 and not torch.is_autocast_enabled():
+            # bf16 on the GPU: the library's q/k prologue (norms and rotary
+            # embedding in one pass) where it applies, then its dense bf16
+            # attention writing token-major rows straight into proj's input
+            from . import kernels as K
+            from .qkv import _fused_prologue
+
+            fused = _fused_prologue(self, lin, pos, nh, hd)
+            if fused is None:
+                q, k, v = lin.view(B, T, 3, nh, hd).permute(2, 0, 3, 1, 4).unbind(0)
+                q, k = self.q_norm(q), self.k_norm(k)
+                if self.rope is not None and pos is not None:
+                    q, k = self.rope(q, pos), self.rope(k, pos)
+                fused = (q.contiguous(), k.contiguous(), v.contiguous())
+            q, k, v = fused
+            o = torch.empty(B, T, C, dtype=x.dtype, device=x.device)
+            K.dense_attn(q.reshape(B * nh, T, hd), k.reshape(B * nh, T, hd), v.reshape(B * nh, T, hd), out=o,
+                         out_rows=(nh, T * C, hd, C, T, 0, 0))
+            return self.proj_drop(self.proj(o))
+        q, k, v = lin.view(B, T, 3, nh, hd).permute(2, 0, 3, 1, 4).unbind(0)
         q, k = self.q_norm(q), self.k_norm(k)
         if self.rope is not None and pos is not None:
             q, k = self.rope(q, pos), self.rope(k, pos)
