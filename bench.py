@@ -54,6 +54,10 @@ def _args():
                     help="the scoring passes (pooling, quantisation, key mean) on the cfg2 layer, for ncu")
     ap.add_argument("--profile-rs", action="store_true",
                     help="restore-swap on the cfg2 layer with 0/1/5 rounds and track-best off/on, for ncu")
+    ap.add_argument("--profile-select", action="store_true",
+                    help="top-m and round-step kernels at the reference's quoted Triton shapes")
+    ap.add_argument("--profile-dense", action="store_true",
+                    help="the dense bf16 attention kernel on frame-attention and special-query shapes")
     ap.add_argument("--eager", action="store_true", help="time eager calls instead of CUDA-graph replays")
     ap.add_argument("--shard", default="heads", choices=["heads", "views"],
                     help="views: frames split over the ranks, K/V all-gathered (whole-model sharding)")
@@ -742,6 +746,7 @@ def run_model(args):
     if ws > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item()) / steps
+    split = _model_op_split(model, images, rank, stream) if ws == 1 else None
     if rank == 0:
         line = {"metric": "VGGT aggregator views/s", "value": N / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
                 "steps": steps, "warmup": max(2, min(args.warmup, 3)), "ms_per_step": ms,
@@ -751,12 +756,153 @@ def run_model(args):
                                        f"sparse_ratio={SPARSE_RATIO}, n_iters=5), HeSS lambda 0.5",
                            "parallelism": f"views over {ws} GPU(s)" + (", NCCL all-gather of K/V per global block"
                                                                         if ws > 1 else "")},
-                "torch_dense_ms_per_step": dense_ms,
+                "dense_global_ms_per_step": dense_ms,
+                "dense_global_note": "the same model with exact dense attention (torch SDPA) in the 24 global "
+                                     "blocks instead of apply_ress",
+                "op_split_ms": split,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def _model_op_split(model, images, rank, stream):
+    """Device time of one aggregator forward by part: CUDA events around the
+    patch encoder and around each block's attention, MLP and the rest of the
+    block (norms, layer scales, residuals), summed per block kind."""
+    agg = model.aggregator
+    spans = []
+
+    def wrap(mod, name):
+        def pre(_m, _a):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            spans.append([name, e, None])
+
+        def post(_m, _a, _o):
+            for sp in reversed(spans):
+                if sp[0] == name and sp[2] is None:
+                    e = torch.cuda.Event(enable_timing=True)
+                    e.record(stream)
+                    sp[2] = e
+                    break
+        return [mod.register_forward_pre_hook(pre), mod.register_forward_hook(post)]
+
+    hooks = wrap(agg.patch_embed, "patch_encoder")
+    for kind, blocks in (("frame", agg.frame_blocks), ("global", agg.global_blocks)):
+        for blk in blocks:
+            hooks += wrap(blk, f"{kind}_block")
+            hooks += wrap(blk.attn, f"{kind}_attention")
+            hooks += wrap(blk.mlp, f"{kind}_mlp")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.inference_mode():
+        e0.record(stream)
+        model(images, first_frame=(rank == 0))
+        e1.record(stream)
+    torch.cuda.synchronize()
+    for h in hooks:
+        h.remove()
+    tot = {}
+    for name, a, b in spans:
+        tot[name] = tot.get(name, 0.0) + a.elapsed_time(b)
+    out = {"total": round(e0.elapsed_time(e1), 2), "patch_encoder": round(tot.get("patch_encoder", 0.0), 2)}
+    for kind in ("frame", "global"):
+        blk, att, mlp = (tot.get(f"{kind}_{x}", 0.0) for x in ("block", "attention", "mlp"))
+        out[f"{kind}_attention"] = round(att, 2)
+        out[f"{kind}_mlp"] = round(mlp, 2)
+        out[f"{kind}_norms_residuals"] = round(blk - att - mlp, 2)
+    out["other"] = round(out["total"] - out["patch_encoder"] - sum(out[f"{k}_{x}"] for k in ("frame", "global")
+                                                                    for x in ("attention", "mlp", "norms_residuals")), 2)
+    out["note"] = "one extra forward with CUDA events around each part (eager; events add small gaps)"
+    return out
+
+
+def profile_select():
+    """The selection kernels at the shapes the reference's Triton kernels are
+    timed on in its sources: top-m masks over 16 x 810 rows of 1,619
+    candidates (src/ress/scoring/fused_topm.py:127-131: 0.344 ms) and one
+    restore-swap round over 16 x 128 rows of 4,096 / 6,476 / 8,192
+    candidates (src/ress/scoring/fused_round.py:55-62: 0.398 / 2.481 / 1.707
+    ms).  Those Triton kernels are not run here: the reference tree is not on
+    the GPU box.  CUDA-event time per call, median of 20 after 3 warm-ups;
+    one JSON line per shape."""
+    from ress_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(20):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    rows, n = 16 * 810, 1619
+    q = torch.rand(rows, n, device=dev, generator=g)
+    cnt = torch.randint(0, n + 1, (rows,), device=dev, generator=g, dtype=torch.int32)
+    ms = timed(lambda: K.top_m_mask(q, cnt))
+    print(json.dumps({"kernel": "ress_top_m_mask", "rows": rows, "n": n, "dtype": "f32", "ms": round(ms, 4),
+                      "reference_triton_ms_quoted": 0.344,
+                      "bytes_GBs": round((rows * n * 5) / (ms / 1e3) / 1e9, 1)}), flush=True)
+    for n, quoted in ((4096, 0.398), (6476, 2.481), (8192, 1.707)):
+        rows = 16 * 128
+        P = torch.rand(rows, n, device=dev, generator=g).bfloat16()
+        tk = torch.rand(rows, n, device=dev, generator=g).bfloat16()
+        ssq = (torch.rand(rows, n, device=dev, generator=g) * 0.01).bfloat16()
+        tq = torch.rand(rows, device=dev, generator=g)
+        drop = torch.rand(rows, n, device=dev, generator=g) < 0.5
+        pic = torch.randint(1, 64, (rows,), device=dev, generator=g, dtype=torch.int32)
+        gn = torch.rand(rows, device=dev, generator=g)
+        km = torch.rand(rows, device=dev, generator=g) + 1.0
+        ms = timed(lambda: K.round_step(P, tk, ssq, tq, drop, pic, True, True, g_norm_sq=gn, kept_mass=km))
+        print(json.dumps({"kernel": "ress_round_step", "rows": rows, "n": n, "dtype": "bf16", "ms": round(ms, 4),
+                          "reference_triton_ms_quoted": quoted,
+                          "bytes_GBs": round((rows * n * 8) / (ms / 1e3) / 1e9, 1)}), flush=True)
+
+
+def profile_dense():
+    """The dense bf16 attention kernel on one frame-attention layer of the
+    32-view aggregator (32 frames x 16 heads = 512 sequences of 1,374 tokens)
+    and on the global layer's special-token queries (16 heads x 160 queries
+    over 43,968 keys); TFLOP/s (4 * Tq * Tk * 64 per sequence) by CUDA
+    events, beside torch's SDPA on the same inputs."""
+    from ress_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    bf16_peak, _, peak_src = _peaks()
+    for name, S, Tq, Tk in (("frame", 512, 1374, 1374), ("special", 16, 160, 43968)):
+        q = torch.randn(S, Tq, 64, device=dev, generator=g).bfloat16()
+        k = torch.randn(S, Tk, 64, device=dev, generator=g).bfloat16()
+        v = torch.randn(S, Tk, 64, device=dev, generator=g).bfloat16()
+        out = torch.empty(S, Tq, 64, device=dev, dtype=torch.bfloat16)
+        flops = 4.0 * Tq * Tk * 64 * S
+
+        def ours():
+            K.dense_attn(q, k, v, out=out)
+
+        def torch_sdpa():
+            torch.nn.functional.scaled_dot_product_attention(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0))
+
+        res = {"case": name, "sequences": S, "Tq": Tq, "Tk": Tk}
+        for tag, fn in (("ress_dense_attn", ours), ("torch_sdpa", torch_sdpa)):
+            for _ in range(3):
+                fn()
+            ms = _time_region(fn, 20, torch.cuda.current_stream(dev)) / 20
+            res[f"{tag}_ms"] = round(ms, 4)
+            res[f"{tag}_tflops"] = round(flops / (ms / 1e3) / 1e12, 1)
+        K.check_status(dev)
+        res["frac_of_bf16_peak"] = round(res["ress_dense_attn_tflops"] / bf16_peak, 3)
+        res["peak_note"] = f"bf16 burst {bf16_peak:.0f} TF/s ({peak_src})"
+        print(json.dumps(res), flush=True)
 
 
 def profile_attn():
@@ -846,6 +992,12 @@ def main():
         return
     if args.profile_rs:
         profile_rs(args.frames)
+        return
+    if args.profile_select:
+        profile_select()
+        return
+    if args.profile_dense:
+        profile_dense()
         return
     if args.profile_score:
         profile_score()
