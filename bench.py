@@ -145,9 +145,8 @@ def _setup(frames, world, rank, device):
     shape = synth.LayerShape(n_frames=frames)
     q, k, v = synth.layer_qkv(shape, seed=0, dtype=torch.bfloat16, device=device)
     H = shape.n_heads
-    if H % world:
+    if world > H:
         raise SystemExit(f"{H} heads do not split over {world} GPUs")
-    hl = H // world
     # HessBudget tables: row 0 (W_Q) of two log-normal (3, 24, 16) tables, lambda = 0.5, layer 0
     cam, pcd = synth.fisher_table(seed=1)[0], synth.fisher_table(seed=3)[0]
     cam = cam / cam.sum(-1, keepdim=True)
@@ -160,9 +159,12 @@ def _setup(frames, world, rank, device):
     if world > 1:
         from ress_b200 import shard as SH
 
-        # heads balanced over the GPUs by their HeSS scores (budgets grow with the score)
-        shard = SH.make_head_shard(H, world, rank, scores=head_scores, cap=1.0 / (1.0 - SPARSE_RATIO))
+        # heads balanced over the GPUs by their expected work (HeSS budgets grow with the
+        # score); ranks may hold different numbers of heads
+        shard = SH.make_head_shard(H, world, rank, scores=head_scores, cap=1.0 / (1.0 - SPARSE_RATIO),
+                                   equal_size=False)
         heads = list(shard.heads)
+    hl = len(heads)
     hidx = torch.as_tensor(heads, dtype=torch.long, device=device)
     q, k, v = (t.index_select(1, hidx).contiguous() for t in (q, k, v))
     L = K.Layout(1, hl, shape.n_frames, shape.n_special, shape.hw)
@@ -506,11 +508,9 @@ def run_ress(args):
     if ws > 1:
         torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
     e_ms = float(te.item())
-    h2d = sum(x.numel() * x.element_size() for x in (qh, kh, vh))
-    d2h = ohs[0].numel() * ohs[0].element_size()
-    if ws > 1:
-        h2d *= ws
-        d2h *= ws
+    # bytes of the whole layer (every rank copies its own heads' share)
+    h2d = sum(x.numel() * x.element_size() for x in (qh, kh, vh)) * S["shape"].n_heads // L.H
+    d2h = ohs[0].numel() * ohs[0].element_size() * S["shape"].n_heads // L.H
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -528,7 +528,9 @@ def run_ress(args):
             "config": {"workload": f"cfg2: one VGGT global-attention layer, {args.frames} views x 1374 tokens, "
                                    f"16 heads x 64, bf16, apply_ress(sparse_ratio={SPARSE_RATIO}, n_iters=5), "
                                    "HeSS budget lambda=0.5",
-                       "parallelism": f"heads split over {ws} GPU(s)" + (", NCCL all-gather of HeSS baselines" if ws > 1 else ""),
+                       "parallelism": f"heads split over {ws} GPU(s)" + (
+                           f" by expected work ({L.H} heads on rank 0), NCCL all-gather of HeSS baselines"
+                           if ws > 1 else ""),
                        "launch": "eager calls" if args.eager else "one CUDA graph replay per step (layer captured once)",
                        "l2": "inputs larger than L2 (Q/K/V bf16 270 MB)", "sparsity": round(sparsity, 4)},
             "stages_ms": stages,
@@ -539,7 +541,7 @@ def run_ress(args):
             "gpu_launches": 12 * args.steps,
             "roofline": {"bound": "tensor", "kernel": "sparse_attn_kernel", "achieved": achieved,
                          "peak": mixed_peak, "unit": "TFLOP/s", "frac": achieved / mixed_peak,
-                         "traffic": ATTN_DRAM_BYTES_PER_LAUNCH * args.frames / N_FRAMES / ws,
+                         "traffic": ATTN_DRAM_BYTES_PER_LAUNCH * args.frames / N_FRAMES * L.H / S["shape"].n_heads,
                          "traffic_note": "dram read+write bytes per launch on this rank (its share of the heads), "
                                          "ncu on the 24-frame layer scaled by tokens",
                          "attn_ms": attn_ms, "attn_tflop_per_launch": attn_flops / 1e12,

@@ -2,8 +2,9 @@
 
 Every stage of the layer is independent per attention head except the HeSS
 budget (budget/_proportional.py:149-215), which re-allocates the baseline
-counts of all heads of a q-block column.  Heads are therefore split evenly
-across ranks, and the only exchange is an all-gather of the (B, H/N, nq)
+counts of all heads of a q-block column.  Heads are therefore split across
+ranks (balanced by their expected work, ranks may hold different numbers of
+heads), and the only exchange is an all-gather of the (B, H_local, nq)
 int32 baselines before ``ress_hess_adjust``, which then runs redundantly on
 every rank over all heads (it is tiny).  The gather uses the list form of
 ``all_gather`` so the same code runs on NCCL and on gloo (CPU tests).
@@ -57,39 +58,103 @@ def budget_shares(scores, cap: float | None = None) -> list:
     return w
 
 
-def balanced_heads(scores, world: int, cap: float | None = None) -> list:
-    """Partition the heads into `world` equal-size groups whose summed
-    expected budgets (``budget_shares``) are as even as a greedy pass makes
-    them (heaviest head first, to the lightest group with room).  The result
-    depends only on the scores, so every rank computes the same one."""
+# Per-head fixed cost of a rank, in units of the attention time of a head with
+# the mean budget: scoring, pooled map, budget and restore-swap cost the same
+# for every head (they run over all its candidates), attention grows with the
+# kept blocks.  Measured on the cfg2 layer on one B200: 1.40 ms of per-head
+# stages and 5.46 ms of attention for 16 heads, 0.0875 / 0.341 = 0.26.
+HEAD_COST = 0.26
+
+
+def balanced_heads(scores, world: int, cap: float | None = None, equal_size: bool = True,
+                   head_cost: float = HEAD_COST) -> list:
+    """Partition the heads over `world` ranks so that the ranks' expected
+    work is even.  equal_size: groups of H / world heads balanced by their
+    summed expected budgets (``budget_shares``), greedily (heaviest head first,
+    to the lightest group with room).  Otherwise groups of any size (at
+    least one head each) balanced by head_cost + budget share per head:
+    longest-processing-time-first, then moves and swaps out of the heaviest
+    group while they lower its load.  The result depends only on the scores,
+    so every rank computes the same one."""
     s = budget_shares(scores, cap)
     H = len(s)
-    if H % world:
-        raise ValueError(f"{H} heads do not split evenly over {world} ranks")
-    per = H // world
+    if equal_size:
+        if H % world:
+            raise ValueError(f"{H} heads do not split evenly over {world} ranks")
+        per = H // world
+        groups = [[] for _ in range(world)]
+        sums = [0.0] * world
+        for h in sorted(range(H), key=lambda i: (-s[i], i)):
+            g = min((i for i in range(world) if len(groups[i]) < per), key=lambda i: (sums[i], i))
+            groups[g].append(h)
+            sums[g] += s[h]
+        return [sorted(g) for g in groups]
+    if world > H:
+        raise ValueError(f"{H} heads cannot give each of {world} ranks one")
+    c = [x + head_cost for x in s]
     groups = [[] for _ in range(world)]
-    sums = [0.0] * world
-    for h in sorted(range(H), key=lambda i: (-s[i], i)):
-        g = min((i for i in range(world) if len(groups[i]) < per), key=lambda i: (sums[i], i))
+    load = [0.0] * world
+    for h in sorted(range(H), key=lambda i: (-c[i], i)):
+        g = min(range(world), key=lambda i: (load[i], i))
         groups[g].append(h)
-        sums[g] += s[h]
+        load[g] += c[h]
+    for _ in range(64 * H):  # each step lowers the maximum load, so this ends long before
+        mx = max(range(world), key=lambda i: (load[i], -i))
+        top = load[mx]
+        best = None  # (new max of the pair, kind, head, other group, other head)
+        for o in range(world):
+            if o == mx:
+                continue
+            for h in groups[mx]:
+                if len(groups[mx]) > 1:
+                    new = max(top - c[h], load[o] + c[h])
+                    if new < top - 1e-12 and (best is None or new < best[0]):
+                        best = (new, h, o, None)
+                for h2 in groups[o]:
+                    d = c[h] - c[h2]
+                    if d > 0:
+                        new = max(top - d, load[o] + d)
+                        if new < top - 1e-12 and (best is None or new < best[0]):
+                            best = (new, h, o, h2)
+        if best is None:
+            break
+        _, h, o, h2 = best
+        groups[mx].remove(h)
+        groups[o].append(h)
+        load[mx] -= c[h]
+        load[o] += c[h]
+        if h2 is not None:
+            groups[o].remove(h2)
+            groups[mx].append(h2)
+            load[o] -= c[h2]
+            load[mx] += c[h2]
     return [sorted(g) for g in groups]
 
 
-def make_gather(world: int, group=None, order=None):
-    """base (B, H_local, nq) int32 -> (B, world * H_local, nq): rank order, or
-    global head order when `order` (the heads of every rank, rank after rank)
-    is given."""
+def make_gather(world: int, group=None, order=None, sizes=None):
+    """base (B, H_local, nq) int32 -> (B, H, nq): rank order, or global head
+    order when `order` (the heads of every rank, rank after rank) is given.
+    sizes: heads per rank when they differ; each rank's part then travels
+    padded to the largest size (all_gather moves equal-size tensors)."""
     inv = None
     if order is not None:
         inv = torch.empty(len(order), dtype=torch.long)
         inv[torch.as_tensor(order, dtype=torch.long)] = torch.arange(len(order))
     on_device = {}  # device copies, made on the first (eager) call: no host copy inside a graph capture
+    uneven = sizes is not None and len(set(sizes)) > 1
+    pad = max(sizes) if uneven else 0
 
     def gather(base: torch.Tensor) -> torch.Tensor:
-        parts = [torch.empty_like(base) for _ in range(world)]
-        dist.all_gather(parts, base.contiguous(), group=group)
-        full = torch.cat(parts, dim=1)
+        if uneven:
+            send = base.new_zeros(base.shape[0], pad, *base.shape[2:])
+            send[:, : base.shape[1]] = base
+            parts = [torch.empty_like(send) for _ in range(world)]
+            dist.all_gather(parts, send, group=group)
+            full = torch.cat([p[:, :n] for p, n in zip(parts, sizes)], dim=1)
+        else:
+            parts = [torch.empty_like(base) for _ in range(world)]
+            dist.all_gather(parts, base.contiguous(), group=group)
+            full = torch.cat(parts, dim=1)
         if inv is not None:
             idx = on_device.get(full.device)
             if idx is None:
@@ -99,15 +164,18 @@ def make_gather(world: int, group=None, order=None):
     return gather
 
 
-def make_head_shard(n_heads: int, world: int, rank: int, group=None, scores=None, cap=None) -> HeadShard:
+def make_head_shard(n_heads: int, world: int, rank: int, group=None, scores=None, cap=None,
+                    equal_size: bool = True, head_cost: float = HEAD_COST) -> HeadShard:
     """Contiguous head ranges, or with `scores` (the layer's HeSS head scores)
-    the balanced partition of ``balanced_heads``."""
+    the balanced partition of ``balanced_heads`` (equal_size=False: ranks
+    may hold different numbers of heads)."""
     if scores is None:
         h0, _ = head_range(n_heads, world, rank)
         return HeadShard(h0=h0, h_total=n_heads, gather=make_gather(world, group))
-    parts = balanced_heads(scores, world, cap)
+    parts = balanced_heads(scores, world, cap, equal_size=equal_size, head_cost=head_cost)
     order = [h for p in parts for h in p]
-    return HeadShard(h0=parts[rank][0], h_total=n_heads, gather=make_gather(world, group, order),
+    return HeadShard(h0=parts[rank][0], h_total=n_heads,
+                     gather=make_gather(world, group, order, sizes=[len(p) for p in parts]),
                      heads=tuple(parts[rank]))
 
 

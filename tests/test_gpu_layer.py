@@ -117,10 +117,12 @@ def test_head_split_equals_full():
         assert (ps - fs).abs().max().item() < 1e-2
 
 
-def test_balanced_head_split_equals_full():
+@pytest.mark.parametrize("equal_size,world", [(True, 4), (False, 5)])
+def test_balanced_head_split_equals_full(equal_size, world):
     """Heads split by the balanced partition (non-contiguous head sets per
-    rank), baselines gathered back into global head order: each rank's
-    lists and patch outputs are the unsplit layer's."""
+    rank, equal or unequal numbers of heads), baselines gathered back into
+    global head order: each rank's lists and patch outputs are the unsplit
+    layer's."""
     from ress_b200 import shard as SH
 
     shape, dtype = synth.LayerShape(n_frames=6), torch.bfloat16
@@ -133,22 +135,24 @@ def test_balanced_head_split_equals_full():
     L = K.Layout(1, 16, shape.n_frames, shape.n_special, shape.hw)
     qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
     full = LY.global_layer(qd, kd, vd, L, budget, LY.OrderSpec("restore_swap", M=M))
-    world = 4
-    parts = SH.balanced_heads(hs, world, cap=2.0)
+    parts = SH.balanced_heads(hs, world, cap=2.0, equal_size=equal_size)
     assert sorted(h for p in parts for h in p) == list(range(16))
-    assert any(p != list(range(p[0], p[0] + 4)) for p in parts)  # not all contiguous
-    Lg = K.Layout(1, 4, shape.n_frames, shape.n_special, shape.hw)
+    assert any(p != list(range(p[0], p[0] + len(p))) for p in parts)  # not all contiguous
+    if not equal_size:
+        assert len({len(p) for p in parts}) > 1
     base_all = torch.empty(1, 16, L.nq, dtype=torch.int32, device=dev)
     for p in parts:
         hidx = torch.as_tensor(p, device=dev)
+        Lg = K.Layout(1, len(p), shape.n_frames, shape.n_special, shape.hw)
         qbar, _, _ = K.pool_quant_q(qd.index_select(1, hidx).contiguous(), Lg, quant=False)
         kbar, _, _, _, _, _ = K.pool_quant_kv(kd.index_select(1, hidx).contiguous(),
                                               vd.index_select(1, hidx).contiguous(), Lg, quant=False)
         _, ac = K.predict(qbar, kbar, Lg.n_cand, full=False)
-        base_all[:, hidx] = K.baseline(ac, 0.5).view(1, 4, -1)
+        base_all[:, hidx] = K.baseline(ac, 0.5).view(1, len(p), -1)
     w = L.n_cand + L.sink_blocks
     for p in parts:
         hidx = torch.as_tensor(p, device=dev)
+        Lg = K.Layout(1, len(p), shape.n_frames, shape.n_special, shape.hw)
         sh = LY.HeadShard(h0=p[0], h_total=16, gather=lambda base, _g=base_all: _g, heads=tuple(p))
         part = LY.global_layer(qd.index_select(1, hidx).contiguous(), kd.index_select(1, hidx).contiguous(),
                                vd.index_select(1, hidx).contiguous(), Lg, budget,

@@ -150,6 +150,44 @@ def test_balanced_head_exchange_four_ranks():
     assert sorted(seen) == list(range(16))
 
 
+def _uneven_worker(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        sh = shard.make_head_shard(16, world, rank, scores=_scores(), cap=2.0, equal_size=False)
+        local = _base().index_select(1, torch.as_tensor(sh.heads)).contiguous()
+        full = sh.gather(local)
+        nts = oracle.hess_adjust(full, oracle.scores_norm(_scores()), 60, min_clamp=2)
+        out_q.put((rank, full.numpy().copy(), sh.select(nts, len(sh.heads)).numpy().copy(), list(sh.heads)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_uneven_head_groups_three_ranks():
+    """Ranks holding different numbers of heads: the padded all-gather returns
+    every head's baselines in global order and each rank keeps its own."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 32500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_uneven_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    res = {r: (f, n, h) for r, f, n, h in (q.get(timeout=120) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = oracle.hess_adjust(_base(), oracle.scores_norm(_scores()), 60, min_clamp=2)
+    seen, sizes = [], []
+    for r in range(3):
+        full, nts, heads = res[r]
+        assert torch.equal(torch.from_numpy(full), _base())
+        assert torch.equal(torch.from_numpy(nts), ref[:, heads])
+        seen += heads
+        sizes.append(len(heads))
+    assert sorted(seen) == list(range(16))
+    assert len(set(sizes)) > 1  # 16 heads over 3 ranks cannot be even
+
+
 def test_budget_shares_cap():
     s = torch.tensor([10.0] + [1.0] * 7)
     w = shard.budget_shares(s, cap=2.0)
