@@ -280,19 +280,26 @@ struct SelectScratch {
 // select with 8-bit digits finds the m-th largest valid key; entries above
 // it are taken, then the first (m - #above) equal entries in index order.
 // Semantics of fused_topm.py:67-80 (m clamped to [0, n_valid]).
-template <int NT>
-__device__ void block_select_top_m(const uint32_t *key, const uint8_t *valid, int n, int m,
+// INV: entry i is valid where mask[i] == 0 (the complement of the mask).
+// ONLY_VALID: sel is written at valid entries only, so that two selections
+// over complementary masks can share one sel array.
+template <int NT, bool INV = false, bool ONLY_VALID = false>
+__device__ void block_select_top_m(const uint32_t *key, const uint8_t *mask, int n, int m,
                                    uint8_t *sel, SelectScratch &sc) {
     const int tid = threadIdx.x;
     const int chunk = (n + NT - 1) / NT;
     const int i0 = tid * chunk, i1 = min(n, i0 + chunk);
+    auto valid = [&](int i) { return INV ? mask[i] == 0 : mask[i] != 0; };
     int nv = 0;
-    for (int i = i0; i < i1; ++i) nv += valid[i] ? 1 : 0;
+    for (int i = i0; i < i1; ++i) nv += valid(i) ? 1 : 0;
     int n_valid = block_sum_int<NT>(nv, sc.red);
     if (m < 0) m = 0;
     if (m >= n_valid || m == 0) {
         bool all = (m > 0);
-        for (int i = i0; i < i1; ++i) sel[i] = (all && valid[i]) ? 1 : 0;
+        for (int i = i0; i < i1; ++i) {
+            const bool v = valid(i);
+            if (!ONLY_VALID || v) sel[i] = (all && v) ? 1 : 0;
+        }
         __syncthreads();
         return;
     }
@@ -308,7 +315,7 @@ __device__ void block_select_top_m(const uint32_t *key, const uint8_t *valid, in
             int bin = -1;
             if (i < i1) {
                 const uint32_t k = key[i];
-                if (valid[i] && (k & pmask) == prefix) bin = (int)((k >> shift) & 255u);
+                if (valid(i) && (k & pmask) == prefix) bin = (int)((k >> shift) & 255u);
             }
             const unsigned peers = __match_any_sync(0xffffffffu, bin);
             if (bin >= 0 && (tid & 31) == __ffs(peers) - 1) atomicAdd(&sc.hist[bin], __popc(peers));
@@ -346,17 +353,18 @@ __device__ void block_select_top_m(const uint32_t *key, const uint8_t *valid, in
     }
     // prefix == threshold key; rem == number of equal entries to take
     int eq = 0;
-    for (int i = i0; i < i1; ++i) eq += (valid[i] && key[i] == prefix) ? 1 : 0;
+    for (int i = i0; i < i1; ++i) eq += (valid(i) && key[i] == prefix) ? 1 : 0;
     int tot;
     int before = block_excl_scan<NT>(eq, sc.red, &tot);
     for (int i = i0; i < i1; ++i) {
         uint8_t s = 0;
-        if (valid[i]) {
+        const bool v = valid(i);
+        if (v) {
             uint32_t k = key[i];
             if (k > prefix) s = 1;
             else if (k == prefix) { s = (before < rem) ? 1 : 0; ++before; }
         }
-        sel[i] = s;
+        if (!ONLY_VALID || v) sel[i] = s;
     }
     __syncthreads();
 }

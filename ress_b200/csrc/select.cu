@@ -114,7 +114,6 @@ __global__ void __launch_bounds__(VT_NT) vbar_terms_kernel(const T *__restrict__
 // ----------------------------------------------------------------- restore-swap
 struct RSShared {
     SelectScratch sc;
-    float Mt[HD * HD];  // M transposed: thread t reads M[t][j] at Mt[j * HD + t], one bank per lane
     float vq[HD], Mvq[HD], g[HD], Mg[HD], Mgb[HD];
     float tm, sum_pd, G, K, J, bestJ, tqb, tqs;
     int flag;
@@ -134,6 +133,25 @@ __device__ __forceinline__ void load_row64(const uint16_t *src, float *v) {
     }
 }
 
+// sum_i w[i] * v[i] over the 64 bf16 values at src (16-byte aligned), one
+// fp32 FMA chain in index order, read 8 values at a time (few registers).
+// The products are v[i] * w[i] in either operand order (FMA is commutative).
+__device__ __forceinline__ float dot64_bf16(const uint16_t *src, const float *w) {
+    const uint4 *p = reinterpret_cast<const uint4 *>(src);
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 u = p[c];
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            acc = __fmaf_rn(w[c * 8 + 2 * i], __uint_as_float(q[i] << 16), acc);
+            acc = __fmaf_rn(w[c * 8 + 2 * i + 1], __uint_as_float(q[i] & 0xffff0000u), acc);
+        }
+    }
+    return acc;
+}
+
 // Candidates per shared-memory stage of the drift chains: DSTAGES stages in
 // a ring, filled with cp.async DSTAGES - 1 chunks ahead of the chain (the
 // lead covers the L2 latency; measured: one chunk ahead left the chain
@@ -145,7 +163,7 @@ __device__ __forceinline__ void load_row64(const uint16_t *src, float *v) {
 // clk per candidate per chain, the 2-byte column loads and their address
 // arithmetic plus two CTA barriers per 32 candidates.)
 constexpr int DCH = 64;
-constexpr int DSTAGES = 4;
+constexpr int DSTAGES = 3;
 constexpr int STAGE_ROW = DCH + 8;
 constexpr int STAGE_BYTES = DSTAGES * HD * STAGE_ROW * 2;
 __device__ __forceinline__ float rs_lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -156,8 +174,10 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_lead() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(DSTAGES - 1) : "memory");
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// chunk c landed when at most DSTAGES - 2 later chunks are still in flight
+__device__ __forceinline__ void cp_async_wait_chunk() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(DSTAGES - 2) : "memory");
 }
 
 // acc[d] = sum_k w(k) * vbar[k][d] for d = tid < 64 as one sequential fp32
@@ -171,7 +191,7 @@ __device__ __forceinline__ void cp_async_wait_lead() {
 // weights come in one 16-byte and one 8-byte load, so the loads of a batch
 // overlap instead of each waiting on the mask byte before it.
 template <bool MASKED>
-__device__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t *vbt, int vt_stride, int n,
+__device__ __noinline__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t *vbt, int vt_stride, int n,
                          uint16_t *stage, float &acc_out, float &total_out) {
     const int tid = threadIdx.x;
     const int nch = (n + DCH - 1) / DCH;
@@ -210,16 +230,20 @@ __device__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t 
         if (c < nch) issue(c);
         cp_async_commit();
     }
+    // One CTA barrier per chunk: after it, chunk c has landed (every thread's
+    // copies) and every thread is done with chunk c - 1, whose stage the
+    // refill issued next (chunk c + DSTAGES - 1) overwrites.
     for (int c = 0; c < nch; ++c) {
+        cp_async_wait_chunk();  // chunk c has landed (this thread's copies)
+        __syncthreads();        // ... and every thread's
         if (c + DSTAGES - 1 < nch) issue(c + DSTAGES - 1);
         cp_async_commit();
-        cp_async_wait_lead();  // chunk c has landed (this thread's copies)
-        __syncthreads();       // ... and every thread's
         const int r0 = c * DCH, rows = min(DCH, n - r0);
         const uint16_t *st = stage + (c % DSTAGES) * HD * STAGE_ROW;
         if (tid < HD) {
             const uint16_t *col = st + tid * STAGE_ROW;
             int r = 0;
+#pragma unroll 2
             for (; r + 8 <= rows; r += 8) {
                 float w[8];
                 weights8(r0 + r, w);
@@ -244,16 +268,21 @@ __device__ void rs_chain(const uint16_t *P, const uint8_t *mask, const uint16_t 
             }
             for (; r < rows; ++r) tot = __fadd_rn(tot, weight1(r0 + r));
         }
-        __syncthreads();
     }
+    // the ring is reused by the next chain: every thread is done with it and
+    // no copy is left in flight
+    cp_async_wait_all();
+    __syncthreads();
     acc_out = acc;
     total_out = tot;
 }
 
 // g, Mg, G = ||g||^2_M and K for the current drop set (projected.py:868-878,
-// 908-920).  vb: bf16 bits (nkp, 64) of this head.  S.Mt holds M transposed.
+// 908-920).  vb: bf16 bits (nkp, 64) of this head.  Mh: this head's M (64 x 64
+// fp32, row-major; thread t reads its row t, 16-byte loads through the
+// read-only path).
 __device__ void rs_drift(RSShared &S, const uint16_t *P, const uint8_t *drop, const uint16_t *vbt, int vt_stride,
-                         int n_cand, uint16_t *stage) {
+                         int n_cand, uint16_t *stage, const float *__restrict__ Mh) {
     const int tid = threadIdx.x;
     float acc, tot;
     rs_chain<true>(P, drop, vbt, vt_stride, n_cand, stage, acc, tot);
@@ -263,9 +292,16 @@ __device__ void rs_drift(RSShared &S, const uint16_t *P, const uint8_t *drop, co
     if (tid < HD) S.g[tid] = __fsub_rn(__fmul_rn(S.sum_pd, S.vq[tid]), S.g[tid]);
     __syncthreads();
     if (tid < HD) {
+        const float4 *mr = reinterpret_cast<const float4 *>(Mh + tid * HD);
         float a = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < HD; ++j) a = __fmaf_rn(S.Mt[j * HD + tid], S.g[j], a);
+#pragma unroll 4
+        for (int j4 = 0; j4 < HD / 4; ++j4) {
+            const float4 m4 = __ldg(mr + j4);
+            a = __fmaf_rn(m4.x, S.g[4 * j4], a);
+            a = __fmaf_rn(m4.y, S.g[4 * j4 + 1], a);
+            a = __fmaf_rn(m4.z, S.g[4 * j4 + 2], a);
+            a = __fmaf_rn(m4.w, S.g[4 * j4 + 3], a);
+        }
         S.Mg[tid] = a;
     }
     __syncthreads();
@@ -279,8 +315,127 @@ __device__ void rs_drift(RSShared &S, const uint16_t *P, const uint8_t *drop, co
     __syncthreads();
 }
 
+// The two selections of a restore-swap round over the whole CTA in one radix
+// pass sequence (the block form of group_select_top_m_dual): A = top-mA of
+// {i : drop[i]}, B = top-mB of {i : !drop[i]}, each exactly
+// block_select_top_m's result; the sets are disjoint, so one array takes
+// both: sel[i] = drop[i] ? A[i] : B[i].  aux: 2 x 256 + 2 ints of shared
+// memory that is dead at this point.
+template <int NT>
+__device__ void block_select_top_m_dual(const uint32_t *key, const uint8_t *drop, int n, int mA, int mB,
+                                        uint8_t *sel, SelectScratch &sc, int *aux) {
+    int *histA = aux, *histB = aux + 256;
+    int *resB = aux + 512;  // bin, remaining of set B
+    const int tid = threadIdx.x;
+    const int chunk = (n + NT - 1) / NT;
+    const int i0 = tid * chunk, i1 = min(n, i0 + chunk);
+    int nvA = 0, nvB = 0;
+    for (int i = i0; i < i1; ++i) {
+        if (drop[i]) ++nvA;
+        else ++nvB;
+    }
+    const int nv = block_sum_int<NT>(nvA | (nvB << 16), sc.red);  // n < 2^16: the counts do not mix
+    const int n_validA = nv & 0xFFFF, n_validB = nv >> 16;
+    if (mA < 0) mA = 0;
+    if (mB < 0) mB = 0;
+    const bool doneA = mA >= n_validA || mA == 0, doneB = mB >= n_validB || mB == 0;
+    uint32_t prefA = 0, prefB = 0, pmask = 0;
+    int remA = mA, remB = mB;
+    if (!(doneA && doneB)) {
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int b = tid; b < 512; b += NT) aux[b] = 0;
+            __syncthreads();
+            for (int j = 0; j < chunk; ++j) {
+                const int i = i0 + j;
+                int bin = -1;
+                if (i < i1) {
+                    const uint32_t k = key[i];
+                    if (drop[i]) {
+                        if (!doneA && (k & pmask) == prefA) bin = (int)((k >> shift) & 255u);
+                    } else if (!doneB && (k & pmask) == prefB) {
+                        bin = 256 + (int)((k >> shift) & 255u);
+                    }
+                }
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (bin >= 0 && (tid & 31) == __ffs(peers) - 1) atomicAdd(&aux[bin], __popc(peers));
+            }
+            __syncthreads();
+            // warp 0 scans set A, warp 1 set B
+            const int w = tid >> 5, l = tid & 31;
+            const bool active = w == 0 ? !doneA : (w == 1 ? !doneB : false);
+            if (active) {
+                const int *hist = w == 0 ? histA : histB;
+                const int rem = w == 0 ? remA : remB;
+                int c[8], sum = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    c[j] = hist[255 - 8 * l - j];
+                    sum += c[j];
+                }
+                int x = sum;
+                for (int o = 1; o < 32; o <<= 1) {
+                    int y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (l >= o) x += y;
+                }
+                const int before = x - sum;
+                if (before < rem && rem <= x) {
+                    int acc = before;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (acc < rem && rem <= acc + c[j]) {
+                            if (w == 0) {
+                                sc.bin = 255 - 8 * l - j;
+                                sc.remaining = rem - acc;
+                            } else {
+                                resB[0] = 255 - 8 * l - j;
+                                resB[1] = rem - acc;
+                            }
+                        }
+                        acc += c[j];
+                    }
+                }
+            }
+            __syncthreads();
+            if (!doneA) {
+                prefA |= ((uint32_t)sc.bin) << shift;
+                remA = sc.remaining;
+            }
+            if (!doneB) {
+                prefB |= ((uint32_t)resB[0]) << shift;
+                remB = resB[1];
+            }
+            pmask |= 255u << shift;
+            __syncthreads();
+        }
+    }
+    int eqA = 0, eqB = 0;
+    for (int i = i0; i < i1; ++i) {
+        const uint32_t k = key[i];
+        if (drop[i]) eqA += (!doneA && k == prefA) ? 1 : 0;
+        else eqB += (!doneB && k == prefB) ? 1 : 0;
+    }
+    int tot;
+    const int bef = block_excl_scan<NT>(eqA | (eqB << 16), sc.red, &tot);
+    int beforeA = bef & 0xFFFF, beforeB = bef >> 16;
+    for (int i = i0; i < i1; ++i) {
+        uint8_t a = 0;
+        const uint32_t k = key[i];
+        if (drop[i]) {
+            if (doneA) a = mA > 0 ? 1 : 0;
+            else if (k > prefA) a = 1;
+            else if (k == prefA) { a = (beforeA < remA) ? 1 : 0; ++beforeA; }
+        } else {
+            if (doneB) a = mB > 0 ? 1 : 0;
+            else if (k > prefB) a = 1;
+            else if (k == prefB) { a = (beforeB < remB) ? 1 : 0; ++beforeB; }
+        }
+        sel[i] = a;
+    }
+    __syncthreads();
+}
+
 template <typename T>
-__global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
+__global__ void __launch_bounds__(SEL_NT, 3) restore_swap_kernel(
     const T *__restrict__ attn, const uint16_t *__restrict__ vb16, const float *__restrict__ tk,
     const float *__restrict__ M, const int32_t *__restrict__ nts, int H, int nq, int nkp, int n_cand,
     int n_iters, Fracs fr, int track_best, uint8_t *__restrict__ drop_out,
@@ -292,21 +447,33 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     const int row = blockIdx.x;
     const int bh = row / nq, h = bh % H;
     const int tid = threadIdx.x;
-    // P and s^2 hold bf16-rounded values: kept as bf16 bits (exact), which
-    // leaves room for the deep vbar stage ring
+    // Shared memory is kept to ~74 KB for 4,278 candidates so that three CTAs
+    // (three rows) share an SM: the drift chains run on 64 of a CTA's 256
+    // threads, and the other rows' warps fill the issue slots meanwhile.
+    // P and s^2 hold bf16-rounded values: kept as bf16 bits (exact); M is
+    // read from global memory; the drop set of the best evaluation is a
+    // bitmask; the two selections of a round share one array (disjoint sets).
     uint16_t *stage = reinterpret_cast<uint16_t *>(dyn);                // DSTAGES x DCH x 64 bf16
     uint16_t *P = reinterpret_cast<uint16_t *>(dyn + STAGE_BYTES);      // nkp bf16
     uint16_t *ssq = P + ((nkp + 7) & ~7);                               // n_cand bf16
     uint32_t *key = reinterpret_cast<uint32_t *>(ssq + ((n_cand + 7) & ~7)); // n_cand (padded to 16 B)
-    uint8_t *drop = reinterpret_cast<uint8_t *>(key + ((n_cand + 3) & ~3)); // n_cand each; drop 16-B aligned
-    uint8_t *best = drop + n_cand;
-    uint8_t *valid = best + n_cand;
-    uint8_t *sel = valid + n_cand;
-    uint8_t *sel2 = sel + n_cand;
+    uint32_t *best = key + ((n_cand + 3) & ~3);                         // (n_cand + 31) / 32 words
+    uint8_t *drop = reinterpret_cast<uint8_t *>(best + (((n_cand + 31) / 32 + 3) & ~3)); // n_cand; 16-B aligned
+    uint8_t *sel = drop + ((n_cand + 15) & ~15);
     const uint16_t *vb = vb16 + (size_t)bh * nkp * HD;
     const uint16_t *vbt = vbT + (size_t)bh * HD * vt_stride;
+    const float *Mh = M + (size_t)h * HD * HD;
+    const int nwords = (n_cand + 31) / 32;
+    // best <- drop, one 32-candidate word per thread step
+    auto save_best = [&]() {
+        for (int w = tid; w < nwords; w += SEL_NT) {
+            uint32_t bits = 0;
+            const int k0 = w * 32, kn = min(32, n_cand - k0);
+            for (int b = 0; b < kn; ++b) bits |= (drop[k0 + b] ? 1u : 0u) << b;
+            best[w] = bits;
+        }
+    };
 
-    for (int i = tid; i < HD * HD; i += SEL_NT) S.Mt[(i & (HD - 1)) * HD + (i >> 6)] = M[(size_t)h * HD * HD + i];
     for (int k = tid; k < nkp; k += SEL_NT) P[k] = bf16bits(DT<T>::load(attn, (size_t)row * nkp + k));
     __syncthreads();
     // dense_reference over all pooled blocks: v_bar_query = P @ v_bar, total = sum(P)
@@ -320,7 +487,7 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     if (tid < HD) {
         float acc = 0.0f;
 #pragma unroll 8
-        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(bf16r(S.Mt[j * HD + tid]), S.vq[j], acc);
+        for (int j = 0; j < HD; ++j) acc = __fmaf_rn(bf16r(__ldg(Mh + tid * HD + j)), S.vq[j], acc);
         S.Mvq[tid] = bf16r(acc);
     }
     __syncthreads();
@@ -333,11 +500,7 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
     // quadratic_deviation, s, s_cut, s^2 (projected.py:780-783)
     const float eps4 = bf16r(1e-4f);
     for (int k = tid; k < n_cand; k += SEL_NT) {
-        float v[HD];
-        load_row64(vb + (size_t)k * HD, v);
-        float acc = 0.0f;
-#pragma unroll
-        for (int i = 0; i < HD; ++i) acc = __fmaf_rn(S.Mvq[i], v[i], acc);
+        const float acc = dot64_bf16(vb + (size_t)k * HD, S.Mvq);
         float cross = bf16r(acc);
         float quad = bf16r(__fsub_rn(S.tqs, bf16r(__fmul_rn(2.0f, cross))));
         quad = bf16r(__fadd_rn(quad, tk[(size_t)bh * n_cand + k]));
@@ -350,22 +513,23 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
         ssq[k] = bf16bits(__fmul_rn(s, s));
         if (s_out) s_out[(size_t)row * n_cand + k] = bf16bits(s);
         key[k] = order_key(s_cut);
-        valid[k] = 1;
+        drop[k] = 0;
     }
     __syncthreads();
     const int nt = nts[row];
-    block_select_top_m<SEL_NT>(key, valid, n_cand, min(nt, n_cand), sel, S.sc);
+    // every candidate valid: the complement of the all-zero drop array
+    block_select_top_m<SEL_NT, true>(key, drop, n_cand, min(nt, n_cand), sel, S.sc);
     for (int k = tid; k < n_cand; k += SEL_NT) drop[k] = sel[k] ? 0 : 1;
     __syncthreads();
     if (track_best) {
-        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage);
+        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage, Mh);
         if (tid == 0) S.bestJ = S.J;
-        for (int k = tid; k < n_cand; k += SEL_NT) best[k] = drop[k];
+        save_best();
         __syncthreads();
     }
     for (int it = 0; it < n_iters; ++it) {
         const int pic = (int)rintf(__fmul_rn(fr.f[it], (float)nt));
-        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage);
+        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage, Mh);
         if (tid == 0) {
             S.flag = (track_best && S.J < S.bestJ) ? 1 : 0;
             if (S.flag) S.bestJ = S.J;
@@ -375,16 +539,11 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
         }
         if (tid < HD) S.Mgb[tid] = bf16r(S.Mg[tid]);
         __syncthreads();
-        if (S.flag)
-            for (int k = tid; k < n_cand; k += SEL_NT) best[k] = drop[k];
+        if (S.flag) save_best();
         const float G = S.G, K = S.K, tqb = S.tqb;
         int nd = 0, nk = 0, ben = 0;
         for (int k = tid; k < n_cand; k += SEL_NT) {
-            float v[HD];
-            load_row64(vb + (size_t)k * HD, v);
-            float acc = 0.0f;
-#pragma unroll
-            for (int j = 0; j < HD; ++j) acc = __fmaf_rn(v[j], S.Mgb[j], acc);
+            const float acc = dot64_bf16(vb + (size_t)k * HD, S.Mgb);
             float tkk = bf16r(acc);
             const float pk = bf16_from_bits(P[k]), sk = bf16_from_bits(ssq[k]);
             float r = bf16r(__fmul_rn(pk, bf16r(__fsub_rn(tkk, tqb))));
@@ -396,7 +555,6 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
             ben |= (dk && rq > 0.0f) ? 1 : 0;
             nd += dk ? 1 : 0;
             nk += dk ? 0 : 1;
-            valid[k] = dk ? 0 : 1;
         }
         const int n_drop = block_sum_int<SEL_NT>(nd, S.sc.red);
         const int n_kept = block_sum_int<SEL_NT>(nk, S.sc.red);
@@ -406,16 +564,18 @@ __global__ void __launch_bounds__(SEL_NT) restore_swap_kernel(
         cnt = min(cnt, n_drop);
         cnt = min(cnt, n_kept);
         if (!beneficial) cnt = 0;
-        block_select_top_m<SEL_NT>(key, drop, n_cand, cnt, sel, S.sc);
-        block_select_top_m<SEL_NT>(key, valid, n_cand, cnt, sel2, S.sc);
-        for (int k = tid; k < n_cand; k += SEL_NT) drop[k] = (uint8_t)((drop[k] && !sel[k]) || sel2[k]);
+        // restored (dropped -> kept) and newly dropped candidates: the two
+        // selections over complementary sets in one pass sequence, one array
+        // (the stage ring is dead here and holds the two histograms)
+        block_select_top_m_dual<SEL_NT>(key, drop, n_cand, cnt, cnt, sel, S.sc, reinterpret_cast<int *>(stage));
+        for (int k = tid; k < n_cand; k += SEL_NT) drop[k] ^= sel[k];
         __syncthreads();
     }
     if (track_best) {
-        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage);
+        rs_drift(S, P, drop, vbt, vt_stride, n_cand, stage, Mh);
         const bool keep_final = S.J < S.bestJ;
         if (!keep_final)
-            for (int k = tid; k < n_cand; k += SEL_NT) drop[k] = best[k];
+            for (int k = tid; k < n_cand; k += SEL_NT) drop[k] = (uint8_t)((best[k >> 5] >> (k & 31)) & 1u);
         __syncthreads();
     }
     if (drop_out)
@@ -1111,7 +1271,8 @@ static size_t rs2_fixed_bytes(int nkp) { return (size_t)rs2_vstride(nkp) * HD * 
 
 static size_t rs_smem(int nkp, int n_cand) {
     return (size_t)STAGE_BYTES + (size_t)((nkp + 7) & ~7) * 2 + (size_t)((n_cand + 7) & ~7) * 2 +
-           (size_t)((n_cand + 3) & ~3) * 4 + (size_t)n_cand * 5;
+           (size_t)((n_cand + 3) & ~3) * 4 + (size_t)(((n_cand + 31) / 32 + 3) & ~3) * 4 +
+           (size_t)((n_cand + 15) & ~15) + (size_t)n_cand;
 }
 
 // The streamed kernel is used when the v2 kernel cannot hold the head's
@@ -1203,6 +1364,8 @@ static int restore_swap_t(const void *attn_full, const void *vbar, const float *
     size_t sm = rs_smem(nkp, n_cand);
     auto kern = restore_swap_kernel<T>;
     set_smem_attr((const void *)kern, sm);
+    // the largest shared-memory carveout, so that three CTAs fit on an SM
+    cudaFuncSetAttribute((const void *)kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     kern<<<rows, SEL_NT, sm, st>>>((const T *)attn_full, vb16, tk, M, nts, H, nq, nkp, n_cand, n_iters,
                                    fr, track_best, drop, s, lists, counts, list_width, sink_blocks, lead,
                                    status, vbT, vt_stride);
