@@ -379,10 +379,12 @@ def run_ress(args):
         step()
     torch.cuda.synchronize()
     K.check_status(device)
-    kept = res.counts.sum().to(torch.float64)
+    # kept blocks and list slots over all ranks (head groups may differ in size)
+    kept = torch.stack([res.counts.sum().to(torch.float64),
+                        torch.tensor(float(res.counts.numel() * res.width), dtype=torch.float64, device=device)])
     if ws > 1:
         torch.distributed.all_reduce(kept)
-    sparsity = 1.0 - float(kept.item()) / float(res.counts.numel() * ws * res.width)
+    sparsity = 1.0 - float(kept[0].item()) / float(kept[1].item())
     attn_flops = _attn_flops(res.lists, res.counts, L)
 
     barrier()

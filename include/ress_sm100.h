@@ -286,10 +286,10 @@ int ress_sparse_attn_sched(const int8_t *q8, const float *qscale, const int8_t *
 /* ress_sparse_attn_sched for launches with few rows (a head split over many
  * GPUs), where rows that keep nearly every block would otherwise set the
  * kernel time on their own: a row longer than split_chunk blocks runs as
- * ceil(count / split_chunk) pieces (at most 4) of its list on separate CTAs,
+ * min(ceil(count / split_chunk), 2) pieces of its list on separate CTAs,
  * and the piece that finishes last merges them in piece order (softmax
  * maxima and sums combined in fp32).  Scratch, all caller-allocated:
- * item_order 4*rows int32; partial rows*4*128*68 fp32, 16-byte aligned;
+ * item_order 2*rows int32; partial rows*2*128*68 fp32, 16-byte aligned;
  * row_done rows int32, zero before the first call (every call leaves it
  * zero).  P is rounded to fp16 per piece, so split rows agree with
  * ress_sparse_attn within the attention tolerance rather than bit for bit.

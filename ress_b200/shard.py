@@ -61,9 +61,12 @@ def budget_shares(scores, cap: float | None = None) -> list:
 # Per-head fixed cost of a rank, in units of the attention time of a head with
 # the mean budget: scoring, pooled map, budget and restore-swap cost the same
 # for every head (they run over all its candidates), attention grows with the
-# kept blocks.  Measured on the cfg2 layer on one B200: 1.40 ms of per-head
-# stages and 5.46 ms of attention for 16 heads, 0.0875 / 0.341 = 0.26.
-HEAD_COST = 0.26
+# kept blocks.  With few heads per GPU the per-head stages no longer fill the
+# SMs and cost more per head than in a full layer (restore-swap of one head of
+# the cfg2 layer: 0.136 ms, of sixteen: 1.16 ms).  Fitted to whole-layer times
+# of head groups of the cfg2 layer on one B200 (groups of 1-4 heads, time =
+# 0.21 + 0.118 * heads + 0.318 * budget share ms): 0.118 / 0.318 = 0.37.
+HEAD_COST = 0.37
 
 
 def balanced_heads(scores, world: int, cap: float | None = None, equal_size: bool = True,
@@ -135,32 +138,45 @@ def make_gather(world: int, group=None, order=None, sizes=None):
     """base (B, H_local, nq) int32 -> (B, H, nq): rank order, or global head
     order when `order` (the heads of every rank, rank after rank) is given.
     sizes: heads per rank when they differ; each rank's part then travels
-    padded to the largest size (all_gather moves equal-size tensors)."""
-    inv = None
-    if order is not None:
-        inv = torch.empty(len(order), dtype=torch.long)
-        inv[torch.as_tensor(order, dtype=torch.long)] = torch.arange(len(order))
-    on_device = {}  # device copies, made on the first (eager) call: no host copy inside a graph capture
-    uneven = sizes is not None and len(set(sizes)) > 1
-    pad = max(sizes) if uneven else 0
+    padded to the largest size.  One all_gather_into_tensor into a
+    (world * B, pad, nq) buffer and one index_select that picks every head's
+    slot in global order: three kernels at most inside a captured step."""
+    if sizes is None:
+        sizes = None if order is None else [len(order) // world] * world
+    on_device = {}  # device copies of the slot index, made on the first (eager) call
+
+    def slot_index(pad: int, h_local: int) -> torch.Tensor:
+        # (rank, slot) of every head in global order, flattened over (rank, slot)
+        sz = sizes if sizes is not None else [h_local] * world
+        flat = []
+        for r, n in enumerate(sz):
+            flat.extend(r * pad + i for i in range(n))
+        idx = torch.as_tensor(flat, dtype=torch.long)
+        if order is not None:
+            inv = torch.empty(len(order), dtype=torch.long)
+            inv[torch.as_tensor(order, dtype=torch.long)] = torch.arange(len(order))
+            idx = idx[inv]
+        return idx
 
     def gather(base: torch.Tensor) -> torch.Tensor:
-        if uneven:
-            send = base.new_zeros(base.shape[0], pad, *base.shape[2:])
-            send[:, : base.shape[1]] = base
-            parts = [torch.empty_like(send) for _ in range(world)]
-            dist.all_gather(parts, send, group=group)
-            full = torch.cat([p[:, :n] for p, n in zip(parts, sizes)], dim=1)
+        B, h_local = base.shape[0], base.shape[1]
+        pad = max(sizes) if sizes is not None else h_local
+        if h_local == pad:
+            send = base.contiguous()
         else:
-            parts = [torch.empty_like(base) for _ in range(world)]
-            dist.all_gather(parts, base.contiguous(), group=group)
-            full = torch.cat(parts, dim=1)
-        if inv is not None:
-            idx = on_device.get(full.device)
-            if idx is None:
-                idx = on_device[full.device] = inv.to(full.device)
-            full = full.index_select(1, idx)
-        return full
+            send = base.new_zeros(B, pad, *base.shape[2:])
+            send[:, :h_local] = base
+        buf = send.new_empty(world * B, *send.shape[1:])  # rank r's part: rows [r*B, (r+1)*B)
+        dist.all_gather_into_tensor(buf, send, group=group)
+        flat = buf.view(world * pad, *base.shape[2:]) if B == 1 else \
+            buf.view(world, B, pad, *base.shape[2:]).transpose(0, 1).reshape(B, world * pad, *base.shape[2:])
+        key = (base.device, pad, h_local)
+        idx = on_device.get(key)
+        if idx is None:
+            idx = on_device[key] = slot_index(pad, h_local).to(base.device)
+        if B == 1:
+            return flat.index_select(0, idx).unsqueeze(0)
+        return flat.index_select(1, idx)
     return gather
 
 

@@ -158,6 +158,10 @@ def _uneven_worker(rank, world, port, out_q):
         local = _base().index_select(1, torch.as_tensor(sh.heads)).contiguous()
         full = sh.gather(local)
         nts = oracle.hess_adjust(full, oracle.scores_norm(_scores()), 60, min_clamp=2)
+        # a batch of two layers: the gather keeps each batch entry's heads apart
+        base2 = torch.cat([_base(), _base().flip(2) + 100], 0)
+        full2 = sh.gather(base2.index_select(1, torch.as_tensor(sh.heads)).contiguous())
+        assert torch.equal(full2, base2)
         out_q.put((rank, full.numpy().copy(), sh.select(nts, len(sh.heads)).numpy().copy(), list(sh.heads)))
     finally:
         dist.destroy_process_group()
@@ -165,7 +169,8 @@ def _uneven_worker(rank, world, port, out_q):
 
 def test_uneven_head_groups_three_ranks():
     """Ranks holding different numbers of heads: the padded all-gather returns
-    every head's baselines in global order and each rank keeps its own."""
+    every head's baselines in global order (also for a batch of two) and each
+    rank keeps its own."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 32500 + os.getpid() % 1000
