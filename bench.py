@@ -85,36 +85,59 @@ def _peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling during the timed region.  The sampler is started
+    and its first sample awaited before the region begins (starting
+    nvidia-smi takes longer than a short region); samples arrive every 10 ms
+    and are timestamped on arrival, and only those that arrive between the
+    start and the end of the region (plus one sampling interval) count."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 10
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
         self.proc = None
+        self.stamped = []  # (arrival time, line)
+        self.t0 = self.t1 = None
+
+    def _reader(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.stamped.append((time.monotonic(), ln))
 
     def __enter__(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.INTERVAL_MS)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+        if self.proc is not None:
+            self.thread = threading.Thread(target=self._reader, daemon=True)
+            self.thread.start()
+            deadline = time.monotonic() + 5.0
+            while not self.stamped and time.monotonic() < deadline and self.proc.poll() is None:
+                time.sleep(0.005)
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
+        self.t1 = time.monotonic()
         if self.proc is not None:
+            time.sleep(self.INTERVAL_MS * 2 / 1000.0)  # the sample taken at the region's end
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
-        else:
-            self.lines = []
+                self.proc.wait()
+            self.thread.join(timeout=5)
+        grace = self.INTERVAL_MS * 1.5 / 1000.0
+        self.lines = [ln for t, ln in self.stamped if self.t0 <= t <= self.t1 + grace]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -131,10 +154,12 @@ class Clocks:
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
+        region_ms = round((self.t1 - self.t0) * 1e3, 1) if self.t0 is not None and self.t1 is not None else None
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0, "region_ms": region_ms}
         sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "region_ms": region_ms}
 
 
 def _setup(frames, world, rank, device):
@@ -510,9 +535,12 @@ def run_ress(args):
     if ws > 1:
         torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
     e_ms = float(te.item())
-    # bytes of the whole layer (every rank copies its own heads' share)
-    h2d = sum(x.numel() * x.element_size() for x in (qh, kh, vh)) * S["shape"].n_heads // L.H
-    d2h = ohs[0].numel() * ohs[0].element_size() * S["shape"].n_heads // L.H
+    # bytes of the whole layer: every rank copies its own heads' share, summed over ranks
+    nb = torch.tensor([float(sum(x.numel() * x.element_size() for x in (qh, kh, vh))),
+                       float(ohs[0].numel() * ohs[0].element_size())], dtype=torch.float64, device=device)
+    if ws > 1:
+        torch.distributed.all_reduce(nb)
+    h2d, d2h = int(nb[0].item()), int(nb[1].item())
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:

@@ -38,3 +38,26 @@ def test_reference_arm_other_ranks_exit_quietly():
     p = _run({"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
     assert p.returncode == 0, p.stderr[-2000:]
     assert p.stdout.strip() == ""
+
+
+def test_clock_sampler_covers_a_short_region(tmp_path, monkeypatch):
+    """The clock sampler waits for nvidia-smi's first sample before the timed
+    region starts, so that a region of a few tens of milliseconds (a short
+    multi-GPU step) still holds samples; samples outside the region do not
+    count.  A stand-in nvidia-smi that starts slowly and prints a line every
+    10 ms."""
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/bin/bash\nsleep 0.3\nwhile true; do echo \"0, 1800, 1965, 500.0, 0x4, Not Active, "
+                    "Not Active, Not Active, Active\"; sleep 0.01; done\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}:{os.environ['PATH']}")
+    sys.path.insert(0, ROOT)
+    import time
+    import bench
+
+    with bench.Clocks(0) as c:
+        time.sleep(0.03)
+    s = c.summary()
+    assert 1 <= s["samples"] <= 8, s
+    assert s["sm_mhz"] == 1800.0 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"]
