@@ -4,7 +4,8 @@ Same entries and meaning as the reference's ``backbones.py`` (``Backbone``
 :24-44, ``BACKBONES`` :130-174): number of sparsifiable global blocks, heads
 per block, and the HeSS lambda each backbone was tuned at.  Loading a
 pretrained checkpoint needs the backbone's own source tree and network
-access; when those are absent ``load`` raises with the reason.  The Fisher
+access; when those are absent ``load`` raises with the reason (Pi3 and DA3
+wiring of a model the caller has built: ``ress_b200.pi3`` / ``ress_b200.da3``).  The Fisher
 tables are read from ``RESS_CALIBRATION_DIR`` (default: ``calibration/``
 beside this file), file names ``fisher_scores_<name>_{pcd,cam_pos}.pt`` as in
 the reference.
@@ -45,11 +46,20 @@ def _unavailable(name, pkg):
     return load
 
 
+def _load_pi3(**kw):
+    from .pi3 import load_pi3
+    return load_pi3(**kw)
+
+
+def _load_da3(**kw):
+    from .da3 import load_da3
+    return load_da3(**kw)
+
+
 BACKBONES = {
     "vggt": Backbone("vggt", n_global_blocks=24, n_heads=16, hess_lam=0.5, load=_unavailable("vggt", "vggt")),
-    "pi3": Backbone("pi3", n_global_blocks=18, n_heads=16, hess_lam=0.0, load=_unavailable("pi3", "pi3")),
-    "da3": Backbone("da3", n_global_blocks=14, n_heads=24, hess_lam=1.0,
-                    load=_unavailable("da3", "depth_anything_3")),
+    "pi3": Backbone("pi3", n_global_blocks=18, n_heads=16, hess_lam=0.0, load=_load_pi3),
+    "da3": Backbone("da3", n_global_blocks=14, n_heads=24, hess_lam=1.0, load=_load_da3),
 }
 
 
