@@ -79,6 +79,22 @@ int ress_qkv_prologue(const void *qkv, int dtype, int B, int T, int H, const flo
                       const float *qn_bias, const float *kn_weight, const float *kn_bias, float eps,
                       const long long *pos, const void *rope_cos, const void *rope_sin, int rope_len,
                       void *q, void *k, void *v, ress_stream_t stream);
+
+/* ress_qkv_prologue fused with the Q half of ress_pool_quant_q for a bf16
+ * global layer of frames = T / (S + HW) frames (S special tokens, then HW
+ * patch tokens each; T must be a multiple of S + HW): the patch tokens' q
+ * is normalised, rotated, pooled and quantised in one pass over the Linear's
+ * output and never written, so the layer skips one write and one read of
+ * its patch queries (qkv.py:25-68 and attention.py:82-100, 226 in one).
+ * Writes k and v as ress_qkv_prologue does, the special tokens' q
+ * compactly as (B, H, frames * S, 64) bf16 (NULL when S == 0), and qbar,
+ * q8, qscale exactly as ress_pool_quant_q on ress_qkv_prologue's q (both
+ * run the same row math: bit-identical). */
+int ress_qkv_prologue_scored(const void *qkv, int B, int T, int H, int S, int HW, const float *qn_weight,
+                             const float *qn_bias, const float *kn_weight, const float *kn_bias, float eps,
+                             const long long *pos, const void *rope_cos, const void *rope_sin, int rope_len,
+                             void *q_special, void *k, void *v, void *qbar, int8_t *q8, float *qscale,
+                             ress_stream_t stream);
 const char *ress_error_string(int code);
 
 /*

@@ -35,6 +35,8 @@ SIGNATURES = {
     "ress_version": (_I, []),
     "ress_check_scale_division": (_I, [_P, _P]),
     "ress_qkv_prologue": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _F, _P, _P, _P, _I, _P, _P, _P, _P]),
+    "ress_qkv_prologue_scored": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _F, _P, _P, _P, _I, _P, _P, _P, _P, _P,
+                                      _P, _P]),
     "ress_error_string": (ctypes.c_char_p, [_I]),
     "ress_workspace_size": (ctypes.c_size_t, [_I, _I, _I, _I]),
     "ress_score_quant": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L,

@@ -25,12 +25,20 @@ from . import criterion as _criterion
 from . import kernels as K
 from .budget import compute_baseline_num_to_select  # noqa: F401  (re-exported, reference location)
 from .layer import OrderSpec, global_layer
-from .qkv import compute_qkv, get_patch_tokens, project_out
+from .qkv import compute_qkv, compute_qkv_scored, get_patch_tokens, project_out
 
 KS_Q = 128
 KS_K = 64
 KBLK = 64
 MIN_NUM_TO_SELECT = 2
+# True: bf16 layers whose q/k norms and rotary embedding the kernels reproduce
+# take the fused prologue (kernels.qkv_prologue_scored: the patch queries pooled
+# and quantised straight from the qkv Linear's output, never written).  Off by
+# default: both routes give the same bits, and on a B200 the prologue and the
+# Q pass are bound by instruction issue, not HBM, so the fused route, which
+# saves 90 MB of traffic at 32 views but issues more instructions, measured
+# slower (0.222 against 0.192 ms per layer)
+FUSED_PROLOGUE = False
 
 if os.environ.get("RESS_SINK_MASS", "0") != "0" or os.environ.get("RESS_SINK_PROTECT", "1") == "0":
     raise RuntimeError("ress_b200 implements the reference defaults RESS_SINK_MASS=0, RESS_SINK_PROTECT=1 only")
@@ -166,8 +174,19 @@ def ress_attention_forward(self, x, pos, num_to_select=None, budget_fn=None, per
     (attention.py:296-659).  Same arguments and return value."""
     if pool_mode != "avg":
         raise NotImplementedError("pool_mode='avg' only")
-    q, k, v, shp = compute_qkv(self, x, pos, num_special_tokens=num_special_tokens, num_heads=num_heads,
+    scored = None
+    if (FUSED_PROLOGUE and not dense and aux_store is None and not retain_output_grad
+            and getattr(self, "ress_view", None) is None):
+        # bf16 layers whose prologue the kernels reproduce: the patch queries are
+        # pooled and quantised straight from the qkv Linear's output (q is never formed)
+        r = compute_qkv_scored(self, x, pos, num_special_tokens=num_special_tokens, num_heads=num_heads,
                                shape=shape)
+        if r is not None:
+            k, v, scored, shp = r
+            q = None
+    if scored is None:
+        q, k, v, shp = compute_qkv(self, x, pos, num_special_tokens=num_special_tokens, num_heads=num_heads,
+                                   shape=shape)
     B, N, P, hd, nh, S = shp["B"], shp["N"], shp["P"], shp["head_dim"], shp["num_heads"], shp["S"]
     L = K.Layout(B, nh, N, S, P - S)
     res = None
@@ -177,18 +196,19 @@ def ress_attention_forward(self, x, pos, num_to_select=None, budget_fn=None, per
     else:
         if hd != 64:
             raise NotImplementedError("the sm_100a kernels take head_dim 64")
-        if q.dtype not in (torch.float32, torch.bfloat16):
-            q, k, v = q.float(), k.float(), v.float()
-        k = k if k.dtype == q.dtype else k.to(q.dtype)
-        v = v if v.dtype == q.dtype else v.to(q.dtype)
+        if q is not None:
+            if q.dtype not in (torch.float32, torch.bfloat16):
+                q, k, v = q.float(), k.float(), v.float()
+            k = k if k.dtype == q.dtype else k.to(q.dtype)
+            v = v if v.dtype == q.dtype else v.to(q.dtype)
         budget = None
         if joint_select_fn is None and perhead_budget_fn is None and budget_fn is not None:
             tag = getattr(budget_fn, "ress_budget", None)
             if tag is not None and hasattr(tag[0], "spec"):
                 b, layer, sr, cdf, beta = tag
-                budget = b.spec(layer, sr, cdf, beta, device=q.device)
+                budget = b.spec(layer, sr, cdf, beta, device=k.device)
                 budget_fn = None
-        order = _order_for(self, block_criterion, hd, nh, q.device)
+        order = _order_for(self, block_criterion, hd, nh, k.device)
         hook = _protect_own_frame_hook(shp, L.n_cand) if protect_own_frame else None
         pbf = None
         if perhead_budget_fn is not None:
@@ -211,7 +231,7 @@ def ress_attention_forward(self, x, pos, num_to_select=None, budget_fn=None, per
         else:
             res = global_layer(q, k, v, L, budget, order, num_to_select=num_to_select,
                                budget_fn=pbf or budget_fn, keep_pooled=aux_store is not None,
-                               joint_select_fn=joint_select_fn, map_hook=hook)
+                               joint_select_fn=joint_select_fn, map_hook=hook, q_scored=scored)
             x_out = res.out
         sparsity = None
     if aux_store is not None:

@@ -369,4 +369,10 @@ __device__ void block_select_top_m(const uint32_t *key, const uint8_t *mask, int
     __syncthreads();
 }
 
+// score.cu: the fused q prologue + Q pass (ress_qkv_prologue_scored)
+int launch_prologue_pool_q(const void *qkv, int B, int T, int H, int S, int HW, const float *qn_weight,
+                           const float *qn_bias, float eps, const long long *pos, const void *rope_cos,
+                           const void *rope_sin, int rope_len, void *qbar, int8_t *q8, float *qscale,
+                           cudaStream_t s);
+
 }  // namespace ress

@@ -13,6 +13,7 @@
 #include <climits>
 
 #include "common.cuh"
+#include "prologue.cuh"
 
 namespace ress {
 
@@ -572,6 +573,118 @@ __global__ void __launch_bounds__(POOL_NT) pool_q_bf16_kernel(
     }
 }
 
+// The q prologue fused into the Q pass (bf16): the tile work of
+// pool_q_bf16_kernel, but each 128-token window's rows are read straight
+// from the qkv Linear's output (B, T, 3 * H * 64) and put through q_norm and
+// the 2-D rotary embedding in registers, so the head-major bf16 q of the
+// patch tokens is never written or read back.  The row math is the
+// prologue kernel's own (prologue_row8, same thread layout: eight threads
+// per row), so the values are its bits.
+__global__ void __launch_bounds__(POOL_NT) prologue_pool_q_kernel(
+    const uint16_t *__restrict__ qkv, int T_, int H, int S, int HW, int Tp, const float *__restrict__ qw,
+    const float *__restrict__ qbias, float eps, const long long *__restrict__ pos, const uint16_t *__restrict__ rcos,
+    const uint16_t *__restrict__ rsin, int rope_len, __nv_bfloat16 *__restrict__ qbar, int8_t *__restrict__ q8,
+    float *__restrict__ qscale, FastDiv fhw) {
+    __shared__ __align__(16) uint16_t tb[KS_Q][72];
+    __shared__ float red[POOL_NT / 32 + 3];
+    const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z, nqb = gridDim.x;
+    const int bh = b * H + h;
+    const int t0 = qb * KS_Q, cnt = min(KS_Q, Tp - t0);
+    const int C = H * HD;
+    const int c = (threadIdx.x & 7) * 8;  // the same head dims in all four rows of this thread
+    // every load of the four rows first (raw values, positions, rotary table
+    // rows), then the row math: the loads of a thread overlap
+    uint4 u[4];
+    long long pa[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int r = (threadIdx.x + k * POOL_NT) >> 3;
+        const bool valid = r < cnt;
+        const long long bt = (long long)b * T_ + patch_tok_f(valid ? t0 + r : t0, S, HW, fhw);
+        u[k] = valid ? ldg16(qkv + bt * 3 * C + (long long)h * HD + c) : make_uint4(0u, 0u, 0u, 0u);
+        pa[k] = rcos != nullptr ? __ldg(pos + bt * 2 + (c >> 5)) : 0;
+    }
+    uint4 cw[4], sw[4];
+    if (rcos != nullptr) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int pax = (int)(pa[k] < 0 ? 0 : (pa[k] >= rope_len ? rope_len - 1 : pa[k]));
+            cw[k] = ldg16(rcos + (size_t)pax * 32 + (c & 31));
+            sw[k] = ldg16(rsin + (size_t)pax * 32 + (c & 31));
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int r = (threadIdx.x + k * POOL_NT) >> 3;
+        float x[8], cs[8] = {}, sn[8] = {};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            x[2 * j] = bf_lo(w_of(u[k], j));
+            x[2 * j + 1] = bf_hi(w_of(u[k], j));
+            if (rcos != nullptr) {
+                cs[2 * j] = bf_lo(w_of(cw[k], j));
+                cs[2 * j + 1] = bf_hi(w_of(cw[k], j));
+                sn[2 * j] = bf_lo(w_of(sw[k], j));
+                sn[2 * j + 1] = bf_hi(w_of(sw[k], j));
+            }
+        }
+        // q_norm and the rotary step (every row of the warp takes part in the
+        // shuffles; rows past the window are zeroed afterwards)
+        prologue_row8<__nv_bfloat16>(x, c, eps, qw, qbias, rcos != nullptr, cs, sn);
+        uint32_t w4[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 hv = __floats2bfloat162_rn(x[2 * j], x[2 * j + 1]);  // exact: already bf16
+            w4[j] = *reinterpret_cast<const uint32_t *>(&hv);
+        }
+        u[k] = r < cnt ? make_uint4(w4[0], w4[1], w4[2], w4[3]) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    // from here on, pool_q_bf16_kernel's tile work on the prologue's values
+    uint32_t m2 = 0u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = threadIdx.x + k * POOL_NT, r = i >> 3, cc = (i & 7) * 8;
+        *reinterpret_cast<uint4 *>(&tb[r][cc]) = u[k];
+        m2 = absmax8(m2, u[k]);
+    }
+    const TileScale ts = block_tile_scale(fmaxf(bf_lo(m2), bf_hi(m2)), red);
+    const float amax = ts.amax;
+    int8_t *dst = q8 + ((size_t)bh * Tp + t0) * HD;
+    if (amax >= 0.0157f && amax < 65520.0f) {
+        const float sc = ts.sc;
+        const QuantScale qs = quant_scale(sc, ts.rc);
+        if (threadIdx.x == 0) qscale[(size_t)bh * nqb + qb] = sc;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = threadIdx.x + k * POOL_NT, r = i >> 3, cc = (i & 7) * 8;
+            if (r >= cnt) continue;
+            const uint4 uk = u[k];
+            *reinterpret_cast<uint2 *>(dst + (size_t)r * 64 + cc) = quant8(
+                [&](int j, float &a, float &bb) {
+                    const uint32_t w = w_of(uk, j);
+                    a = bf_lo(w);
+                    bb = bf_hi(w);
+                },
+                qs);
+        }
+    } else {
+        q_tile_outside(u[0], u[1], u[2], u[3], amax, cnt, dst, qscale + (size_t)bh * nqb + qb);
+    }
+    if (threadIdx.x < HD / 2) {
+        const int d = 2 * threadIdx.x;
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll 8
+        for (int r = 0; r < cnt; ++r) {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(&tb[r][d]);
+            s0 = __fadd_rn(s0, bf_lo(w));
+            s1 = __fadd_rn(s1, bf_hi(w));
+        }
+        const size_t o = ((size_t)bh * nqb + qb) * HD + d;
+        qbar[o] = __float2bfloat16_rn(__fdiv_rn(s0, (float)cnt));
+        qbar[o + 1] = __float2bfloat16_rn(__fdiv_rn(s1, (float)cnt));
+    }
+}
+
 // Pass over K or V (bf16), one 64-key tile per CTA.  K: pooled K and the
 // block sums of fp16(K) for the key mean; V: pooled V and fp16 V.  K and V
 // are separate passes so that the K quantisation, which runs right after
@@ -1026,6 +1139,19 @@ static int pool_quant_q_t(const void *q, int B, int H, int frames, int S, int HW
         pool_q_kernel<T><<<dim3(nqb, BH), POOL_NT, 0, s>>>((const T *)q, H, S, HW, Tp, sb, sh, st, (T *)qbar, q8,
                                                           qscale);
     }
+    return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
+}
+
+// The fused q prologue + Q pass (prologue_pool_q_kernel) for a bf16 layer.
+int launch_prologue_pool_q(const void *qkv, int B, int T, int H, int S, int HW, const float *qn_weight,
+                           const float *qn_bias, float eps, const long long *pos, const void *rope_cos,
+                           const void *rope_sin, int rope_len, void *qbar, int8_t *q8, float *qscale,
+                           cudaStream_t s) {
+    const int frames = T / (S + HW), Tp = frames * HW, nqb = (Tp + KS_Q - 1) / KS_Q;
+    if ((long long)nqb * B * H > INT_MAX) return RESS_E_SHAPE;
+    prologue_pool_q_kernel<<<dim3(nqb, H, B), POOL_NT, 0, s>>>(
+        (const uint16_t *)qkv, T, H, S, HW, Tp, qn_weight, qn_bias, eps, pos, (const uint16_t *)rope_cos,
+        (const uint16_t *)rope_sin, rope_len, (__nv_bfloat16 *)qbar, q8, qscale, make_fastdiv(HW));
     return cudaGetLastError() == cudaSuccess ? RESS_OK : RESS_E_LAUNCH;
 }
 

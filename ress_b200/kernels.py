@@ -149,6 +149,43 @@ def pool_quant_q(q, L: Layout, pool=True, quant=True):
     return qbar, q8, qs
 
 
+def qkv_prologue_scored(qkv, L: Layout, qn_weight=None, qn_bias=None, kn_weight=None, kn_bias=None, eps=1e-5,
+                        pos=None, rope_cos=None, rope_sin=None):
+    """bf16 (B, T, 3*H*64) qkv Linear output of a global layer (layout L) ->
+    dict(k, v: (B, H, T, 64) bf16; q_special: (B*H, frames*S, 64) bf16 or
+    None; qbar, q8, qs as pool_quant_q on qkv_prologue's q).  The patch
+    tokens' q is normalised, rotated, pooled and quantised in one pass and
+    never written (ress_qkv_prologue_scored)."""
+    _dev_ok(qkv)
+    B, T, C3 = qkv.shape
+    H = L.H
+    if qkv.dtype != torch.bfloat16 or C3 != 3 * H * HD or not qkv.is_contiguous():
+        raise RessError("qkv must be contiguous bf16 (B, T, 3*H*64)")
+    if B != L.B or T != L.frames * (L.special + L.hw):
+        raise RessError("qkv does not hold the layout's tokens")
+    dev = qkv.device
+    k, v = (torch.empty(B, H, T, HD, dtype=qkv.dtype, device=dev) for _ in range(2))
+    q_special = torch.empty(B * H, L.frames * L.special, HD, dtype=qkv.dtype, device=dev) if L.special else None
+    qbar = torch.empty(B * H, L.nq, HD, dtype=qkv.dtype, device=dev)
+    q8 = torch.empty(B * H, L.Tp, HD, dtype=torch.int8, device=dev)
+    qs = torch.empty(B * H, L.nq, dtype=torch.float32, device=dev)
+    f32 = lambda t: None if t is None else t.detach().to(device=dev, dtype=torch.float32).contiguous()
+    qw, qb, kw, kb = f32(qn_weight), f32(qn_bias), f32(kn_weight), f32(kn_bias)
+    rope_len = 0
+    if rope_cos is not None:
+        rope_cos, rope_sin = rope_cos.contiguous(), rope_sin.contiguous()
+        if rope_cos.dtype != qkv.dtype or rope_cos.shape[-1] != 32:
+            raise RessError("rotary tables must be (max_pos, 32) in the qkv dtype")
+        rope_len = rope_cos.shape[0]
+        pos = pos.to(dtype=torch.int64).contiguous()
+    check(_lib.load().ress_qkv_prologue_scored(_ptr(qkv), B, T, H, L.special, L.hw, _ptr(qw), _ptr(qb), _ptr(kw),
+                                               _ptr(kb), ctypes.c_float(eps), _ptr(pos), _ptr(rope_cos),
+                                               _ptr(rope_sin), rope_len, _ptr(q_special), _ptr(k), _ptr(v),
+                                               _ptr(qbar), _ptr(q8), _ptr(qs), _stream(dev)),
+          "ress_qkv_prologue_scored")
+    return dict(k=k, v=v, q_special=q_special, qbar=qbar, q8=q8, qs=qs)
+
+
 def pool_quant_kv(k, v, L: Layout, pool=True, quant=True, ws=None):
     _dev_ok(k, v)
     if k.stride() != v.stride() or k.dtype != v.dtype:

@@ -135,16 +135,26 @@ def _random_gen(device):
     return g
 
 
-def special_attention(q, k, v, L: K.Layout, out=None):
+def special_attention(q, k, v, L: K.Layout, out=None, q_special=None):
     """Dense attention of the special-token queries over all keys
     (attention.py:404-409; the key order does not change a softmax).
     bf16 layers with an fp32 full-layout ``out``: the library's dense bf16
     kernel writes the rows straight into their places in ``out`` and None is
     returned.  Otherwise (fp32 layers) torch SDPA's result is returned for
-    the caller to place."""
+    the caller to place.  q_special: the special queries alone, (B*H,
+    frames*special, 64) bf16 (the fused prologue's output), instead of q."""
     if L.special == 0:
         return None
     B, H = L.B, L.H
+    if q_special is not None:
+        if k.dtype != torch.bfloat16 or out is None or out.dtype != torch.float32 or out.stride(-1) != 1:
+            raise K.RessError("special queries from the fused prologue take a bf16 layer and an fp32 output")
+        k2, v2 = k.flatten(0, 1), v.flatten(0, 1)
+        if k2.stride() != v2.stride():
+            k2, v2 = k2.contiguous(), v2.contiguous()
+        rows = (H, out.stride(0), out.stride(1), out.stride(2), L.special, L.special + L.hw, 0)
+        K.dense_attn(q_special, k2, v2, out=out, out_rows=rows)
+        return None
     qs = q.view(B, H, L.frames, L.special + L.hw, 64)[:, :, :, : L.special]
     if q.dtype == torch.bfloat16 and out is not None and out.dtype == torch.float32 and out.stride(-1) == 1:
         q2 = qs.reshape(B * H, L.Ts, 64)  # gathers the special rows (small)
@@ -206,14 +216,17 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
                  num_to_select: torch.Tensor | None = None, budget_fn=None, keep_pooled: bool = False,
                  lead_blocks: int = 0, out: torch.Tensor | None = None,
                  shard: HeadShard | None = None, joint_select_fn=None, map_hook=None,
-                 attn_split=False) -> LayerResult:
+                 attn_split=False, q_scored: dict | None = None) -> LayerResult:
     """Run one sparse global-attention layer.  q, k, v: (B, H, N*P, 64) CUDA,
     float32 or bfloat16.  Exactly one of ``budget``, ``num_to_select`` (a
     (B, H, nq) tensor) or ``budget_fn`` (callable(attn_cond) -> (B, H, nq))
     decides the per-row block count.  ``attn_split`` is the attention's
     ``split`` option (kernels.sparse_attn): None lets a layer with few rows
-    (a head split over many GPUs) spread its longest rows over two CTAs."""
-    dev = q.device
+    (a head split over many GPUs) spread its longest rows over two CTAs.
+    ``q_scored``: the fused prologue's output (kernels.qkv_prologue_scored:
+    the patch queries pooled and quantised, the special queries apart); q is
+    then None and the layer's own Q pass is skipped."""
+    dev = k.device
     if k.stride() != v.stride():
         v = v.contiguous()
         k = k.contiguous()
@@ -226,14 +239,19 @@ def global_layer(q, k, v, L: K.Layout, budget: BudgetSpec | None, order: OrderSp
     capturing = torch.cuda.is_current_stream_capturing()
     side = _side_stream(dev)
     side.wait_stream(main)
+    q_special = None if q_scored is None else q_scored["q_special"]
     with torch.cuda.stream(side):
         # special rows of `out` (disjoint from the patch rows the main stream writes)
-        x_special = special_attention(q, k, v, L, out)
+        x_special = special_attention(q, k, v, L, out, q_special=q_special)
     if not capturing:
-        for t in (q, k, v, out):
-            t.record_stream(side)
+        for t in (q, k, v, out, q_special):
+            if t is not None:
+                t.record_stream(side)
 
-    qbar, q8, qs = K.pool_quant_q(q, L)
+    if q_scored is None:
+        qbar, q8, qs = K.pool_quant_q(q, L)
+    else:
+        qbar, q8, qs = q_scored["qbar"], q_scored["q8"], q_scored["qs"]
     kbar, vbar, k8, ks, v16, km = K.pool_quant_kv(k, v, L, ws=ws)
     need_full = order.kind == "restore_swap" or keep_pooled
     attn_full, attn_cond = K.predict(qbar, kbar, n_cand, full=need_full, cond=True)

@@ -31,10 +31,10 @@ def _fusable_norm(m, hd):
             and m.bias is not None)
 
 
-def _fused_prologue(self, qkv, pos, nh, hd):
-    """q, k, v from the sm_100a prologue kernel when the block's norms and
-    rotary embedding are ones it reproduces (64-dim affine LayerNorm; this
-    package's 2-D table RoPE or none), else None (torch path below)."""
+def _prologue_args(self, qkv, pos, hd):
+    """The prologue kernel's norm and rotary arguments when the block's norms
+    and rotary embedding are ones it reproduces (64-dim affine LayerNorm;
+    this package's 2-D table RoPE or none), else None (torch path)."""
     if not qkv.is_cuda or qkv.dtype not in (torch.float32, torch.bfloat16) or hd != 64:
         return None
     if torch.is_autocast_enabled() or not (_fusable_norm(self.q_norm, hd) and _fusable_norm(self.k_norm, hd)):
@@ -49,10 +49,39 @@ def _fused_prologue(self, qkv, pos, nh, hd):
         cos, sin = rope._cos_sin(hd // 2, rope.MAX_POS, qkv.device, qkv.dtype)
     if self.q_norm.eps != self.k_norm.eps:
         return None
+    return dict(qn_weight=self.q_norm.weight, qn_bias=self.q_norm.bias, kn_weight=self.k_norm.weight,
+                kn_bias=self.k_norm.bias, eps=self.q_norm.eps, pos=pos if cos is not None else None,
+                rope_cos=cos, rope_sin=sin)
+
+
+def _fused_prologue(self, qkv, pos, nh, hd):
+    """q, k, v from the sm_100a prologue kernel (see _prologue_args), else None."""
+    args = _prologue_args(self, qkv, pos, hd)
+    if args is None:
+        return None
     from . import kernels as K
 
-    return K.qkv_prologue(qkv.contiguous(), nh, self.q_norm.weight, self.q_norm.bias, self.k_norm.weight,
-                          self.k_norm.bias, eps=self.q_norm.eps, pos=pos, rope_cos=cos, rope_sin=sin)
+    return K.qkv_prologue(qkv.contiguous(), nh, **args)
+
+
+def compute_qkv_scored(self, x, pos, num_special_tokens=5, num_heads=16, shape=None):
+    """For a bf16 layer whose prologue the kernels reproduce: (k, v, scored,
+    shp) with the patch queries already pooled and quantised by the fused
+    prologue (kernels.qkv_prologue_scored; q itself is never formed), else
+    None."""
+    shp = layer_shape(x, pos, num_special_tokens, num_heads, shape)
+    nh, hd = num_heads, x.shape[-1] // num_heads
+    if x.dtype != torch.bfloat16 or self.qkv.weight.dtype != torch.bfloat16:
+        return None
+    args = _prologue_args(self, x, pos, hd)  # x: the Linear's output has its device and dtype
+    if args is None:
+        return None
+    lin = self.qkv(x)
+    from . import kernels as K
+
+    L = K.Layout(shp["B"], nh, shp["N"], shp["S"], shp["P"] - shp["S"])
+    scored = K.qkv_prologue_scored(lin.contiguous(), L, **args)
+    return scored["k"], scored["v"], scored, shp
 
 
 def compute_qkv(self, x, pos, num_special_tokens=5, num_heads=16, shape=None):

@@ -94,3 +94,84 @@ def test_prologue_without_rope_and_compute_qkv_route():
         qr, kr, _ = lin.view(B, T, 3, a.num_heads, 64).permute(2, 0, 3, 1, 4).unbind(0)
         qr = a.q_norm(qr)
         assert (q2 == qr).float().mean().item() >= 0.97
+
+
+def _inputs_s(a, frames, h, w, S, dtype):
+    g = torch.Generator(device="cuda").manual_seed(11)
+    T = frames * (h * w + S)
+    x = torch.randn(1, T, a.qkv.in_features, device="cuda", generator=g).to(dtype)
+    ys, xs = torch.meshgrid(torch.arange(h, device="cuda"), torch.arange(w, device="cuda"), indexing="ij")
+    patch = torch.stack([ys.reshape(-1), xs.reshape(-1)], dim=-1) + 1
+    frame = torch.cat([torch.zeros(S, 2, dtype=patch.dtype, device="cuda"), patch], dim=0)
+    return x, frame.repeat(frames, 1).reshape(1, T, 2)
+
+
+@pytest.mark.parametrize("frames,h,w,S,heads,rope,affine", [
+    (3, 8, 8, 5, 4, True, True),        # 192 patch tokens: a ragged second window
+    (2, 37, 37, 5, 4, True, True),      # windows that straddle frames
+    (4, 10, 13, 1, 24, True, True),     # DA3's one special token and 24 heads
+    (2, 16, 16, 0, 4, False, True),     # no special tokens, no rotary embedding
+    (3, 9, 9, 5, 4, True, False),       # LayerNorm without weight and bias
+])
+def test_prologue_scored_equals_prologue_then_q_pass(frames, h, w, S, heads, rope, affine):
+    """ress_qkv_prologue_scored (the q prologue fused into the Q pass) gives
+    the bits of ress_qkv_prologue followed by ress_pool_quant_q: k, v, the
+    special queries, the pooled queries, int8 Q and its scales."""
+    from ress_b200 import kernels as K
+
+    a = _attn(torch.bfloat16, dim=heads * 64, heads=heads)
+    if not rope:
+        a.rope = None
+    x, pos = _inputs_s(a, frames, h, w, S, torch.bfloat16)
+    L = K.Layout(1, heads, frames, S, h * w)
+    with torch.inference_mode():
+        lin = a.qkv(x).contiguous()
+        args = Q._prologue_args(a, lin, pos, 64)
+        assert args is not None
+        if not affine:
+            args.update(qn_weight=None, qn_bias=None, kn_weight=None, kn_bias=None)
+        q, k, v = K.qkv_prologue(lin, heads, **args)
+        qbar, q8, qs = K.pool_quant_q(q, L)
+        sc = K.qkv_prologue_scored(lin, L, **args)
+    torch.cuda.synchronize()
+    assert torch.equal(sc["k"], k) and torch.equal(sc["v"], v)
+    assert torch.equal(sc["qbar"], qbar) and torch.equal(sc["q8"], q8) and torch.equal(sc["qs"], qs)
+    if S:
+        special = q.view(1, heads, frames, S + h * w, 64)[:, :, :, :S].reshape(heads, frames * S, 64)
+        assert torch.equal(sc["q_special"], special)
+    else:
+        assert sc["q_special"] is None
+
+
+def test_attention_forward_takes_the_fused_route_bit_identically(monkeypatch):
+    """ress_attention_forward on a bf16 block with LayerNorm q/k norms and the
+    2-D rotary embedding runs the fused prologue (q never formed) and returns
+    exactly what the unfused route (prologue, then the layer's own Q pass)
+    returns."""
+    from ress_b200 import attention as A
+    from ress_b200 import kernels as K
+
+    a = _attn(torch.bfloat16, dim=1024, heads=16)
+    frames, h, w = 4, 16, 16
+    x, pos = _inputs_s(a, frames, h, w, 5, torch.bfloat16)
+    L = K.Layout(1, 16, frames, 5, h * w)
+    nts = torch.full((1, 16, L.nq), max(2, L.n_cand // 2), dtype=torch.int32, device="cuda")
+    calls = []
+    real = A.compute_qkv_scored
+
+    def spy(*args, **kw):
+        r = real(*args, **kw)
+        calls.append(r is not None)
+        return r
+
+    kw = dict(num_to_select=nts, num_special_tokens=5, num_heads=16, block_criterion="probability")
+    monkeypatch.setattr(A, "FUSED_PROLOGUE", True)
+    with torch.inference_mode():
+        monkeypatch.setattr(A, "compute_qkv_scored", spy)
+        fused = A.ress_attention_forward(a, x, pos, **kw)
+        monkeypatch.setattr(A, "FUSED_PROLOGUE", False)
+        plain = A.ress_attention_forward(a, x, pos, **kw)
+    torch.cuda.synchronize()
+    K.check_status()
+    assert calls == [True]
+    assert torch.equal(fused, plain)
