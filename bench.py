@@ -662,28 +662,44 @@ def run_sweep(args):
     """The block-sparse attention op alone (config 5): Tp queries = Tk keys in
     8K..300K, random per-(head, q-block) keep maps at densities 0.1..0.9,
     16 heads x 64, bf16 inputs quantised like the layer.  One JSON line per
-    point; kernel time by CUDA events over `--steps` launches."""
+    point; kernel time by CUDA events over `--steps` launches.  Under
+    torchrun the heads are split over the GPUs (16 / N each, no exchange:
+    every (head, q-block) row is independent) and the time is the maximum
+    over ranks; TFLOP/s count the kept blocks of all ranks."""
     from ress_b200 import kernels as K
 
-    device = torch.device("cuda", 0)
+    ws, rank, local = _dist()
+    device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        if 16 % ws:
+            raise SystemExit(f"16 heads do not split over {ws} GPUs")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    H = 16
+    hl = H // ws
+    h0 = rank * hl
     stream = torch.cuda.current_stream(device)
     bf16_peak, _, peak_src = _peaks()
     int8_peak = _int8_peak(device)
     mixed = 2.0 / (1.0 / bf16_peak + 1.0 / int8_peak)
-    g = torch.Generator(device=device).manual_seed(0)
+    g = torch.Generator(device=device).manual_seed(0)  # every rank draws the full op, then keeps its heads
     for T in (8192, 32768, 131072, 300032):
-        q, k, v = (torch.randn(1, 16, T, 64, device=device, generator=g, dtype=torch.float32).to(torch.bfloat16)
+        q, k, v = (torch.randn(1, H, T, 64, device=device, generator=g, dtype=torch.float32).to(torch.bfloat16)
                    for _ in range(3))
+        q, k, v = (t[:, h0:h0 + hl].contiguous() for t in (q, k, v))
         L = K.Layout.plain(q)
         _, q8, qs = K.pool_quant_q(q, L, pool=False)
         _, _, k8, ks, v16, _ = K.pool_quant_kv(k, v, L, pool=False)
         del q, k, v
         nq, nkb = L.nq, L.nkb
         for dens in (0.1, 0.5, 0.9):
-            m = torch.rand(16 * nq, nkb, device=device, generator=g) < dens
+            m = torch.rand(H * nq, nkb, device=device, generator=g) < dens
+            m = m[h0 * nq:(h0 + hl) * nq].contiguous()
             lists, counts = K.map_to_lists(m)
-            out = torch.empty(16, T, 64, dtype=torch.float32, device=device)
+            out = torch.empty(hl, T, 64, dtype=torch.float32, device=device)
 
             def call():
                 K.sparse_attn(q8, qs, k8, ks, v16, lists, counts, out=out)
@@ -691,18 +707,33 @@ def run_sweep(args):
             for _ in range(3):
                 call()
             steps = max(3, min(args.steps, 20))
+            torch.cuda.synchronize()
+            if ws > 1:
+                torch.distributed.barrier()
             ms = _time_region(call, steps, stream) / steps
             K.check_status(device)
-            flops = 4.0 * 128 * 64 * 64 * float(counts.sum().item())
+            t = torch.tensor([ms, float(counts.sum().item())], dtype=torch.float64, device=device)
+            if ws > 1:
+                mx = t[:1].clone()
+                torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+                torch.distributed.all_reduce(t)
+                t[0] = mx[0]
+            ms, kept = float(t[0].item()), float(t[1].item())
+            flops = 4.0 * 128 * 64 * 64 * kept
             tf = flops / (ms / 1e3) / 1e12
-            print(json.dumps({"metric": "block-sparse attention op (config 5)", "Tp": T, "density": dens,
-                              "kept_blocks": int(counts.sum().item()), "ms": round(ms, 4),
-                              "tflops": round(tf, 1), "frac": round(tf / mixed, 4),
-                              "peak_note": f"mixed peak {mixed:.0f} TF/s: bf16 {bf16_peak:.0f} ({peak_src}), int8 "
-                                           f"{int8_peak:.0f} (measured)"}), flush=True)
+            if rank == 0:
+                print(json.dumps({"metric": "block-sparse attention op (config 5)", "Tp": T, "density": dens,
+                                  "n_gpus": ws, "heads_per_gpu": hl, "kept_blocks": int(kept), "ms": round(ms, 4),
+                                  "tflops": round(tf, 1), "frac": round(tf / (mixed * ws), 4),
+                                  "peak_note": f"mixed peak {mixed:.0f} TF/s per GPU: bf16 {bf16_peak:.0f} "
+                                               f"({peak_src}), int8 {int8_peak:.0f} (measured); frac against "
+                                               f"{ws} x that"}), flush=True)
             del lists, counts, m, out
         del q8, qs, k8, ks, v16
         torch.cuda.empty_cache()
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
 
 
 def run_model(args):
