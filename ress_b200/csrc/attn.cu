@@ -885,6 +885,41 @@ __global__ void __launch_bounds__(NT, 2) sparse_attn_kernel(
 // order: a row's output does not depend on which CTA computes it).
 constexpr int ORDER_NT = 1024;
 constexpr int ORDER_MAX_WIDTH = 16384;
+// Histogram bins -> start offsets in descending bin order (pos[c] = number
+// of entries in bins above c), over the whole CTA: each thread sums a run of
+// consecutive bins from the top, a block-wide exclusive scan places the
+// runs, then each thread writes its run's offsets.
+__device__ __forceinline__ void bins_to_offsets_desc(int *pos, int nb) {
+    __shared__ int wsum[ORDER_NT / 32];
+    const int per = (nb + ORDER_NT - 1) / ORDER_NT;
+    const int i0 = threadIdx.x * per, i1 = min(nb, i0 + per);  // positions from the top bin
+    int local = 0;
+    for (int i = i0; i < i1; ++i) local += pos[nb - 1 - i];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int x = local;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int v = wsum[lane];
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += y;
+        }
+        wsum[lane] = v;  // inclusive over warps
+    }
+    __syncthreads();
+    int run = x - local + (w > 0 ? wsum[w - 1] : 0);  // entries before this thread's run
+    for (int i = i0; i < i1; ++i) {
+        const int c = nb - 1 - i, n = pos[c];
+        pos[c] = run;
+        run += n;
+    }
+    __syncthreads();
+}
 __global__ void __launch_bounds__(ORDER_NT) row_order_kernel(const int32_t *__restrict__ counts, int rows,
                                                               int list_width, int32_t *__restrict__ order) {
     extern __shared__ int pos[];  // list_width + 1 bins
@@ -893,15 +928,7 @@ __global__ void __launch_bounds__(ORDER_NT) row_order_kernel(const int32_t *__re
     __syncthreads();
     for (int r = threadIdx.x; r < rows; r += ORDER_NT) atomicAdd(&pos[min(max(counts[r], 0), list_width)], 1);
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int c = list_width; c >= 0; --c) {  // descending: largest counts first
-            const int n = pos[c];
-            pos[c] = acc;
-            acc += n;
-        }
-    }
-    __syncthreads();
+    bins_to_offsets_desc(pos, nb);  // descending: largest counts first
     for (int r = threadIdx.x; r < rows; r += ORDER_NT)
         order[atomicAdd(&pos[min(max(counts[r], 0), list_width)], 1)] = r;
 }
@@ -927,15 +954,7 @@ __global__ void __launch_bounds__(ORDER_NT) item_order_kernel(const int32_t *__r
     __syncthreads();
     for (int i = threadIdx.x; i < SPLIT_MAX * rows; i += ORDER_NT) atomicAdd(&pos[len(i)], 1);
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int c = list_width; c >= 0; --c) {
-            const int n = pos[c];
-            pos[c] = acc;
-            acc += n;
-        }
-    }
-    __syncthreads();
+    bins_to_offsets_desc(pos, nb);
     for (int i = threadIdx.x; i < SPLIT_MAX * rows; i += ORDER_NT) order[atomicAdd(&pos[len(i)], 1)] = i;
 }
 
