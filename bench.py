@@ -87,14 +87,14 @@ def _peaks():
 class Clocks:
     """nvidia-smi sampling during the timed region.  The sampler is started
     and its first sample awaited before the region begins (starting
-    nvidia-smi takes longer than a short region); samples arrive every 10 ms
+    nvidia-smi takes longer than a short region); samples arrive every 25 ms
     and are timestamped on arrival, and only those that arrive between the
     start and the end of the region (plus one sampling interval) count."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    INTERVAL_MS = 10
+    INTERVAL_MS = int(os.environ.get("RESS_BENCH_CLOCK_MS", "25"))
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
